@@ -1,0 +1,108 @@
+/*
+ * ZipServ TCA-TBE C ABI (ABI version 2) for the B200 library
+ * zipserv_asplos26_b200/_lib/libzipserv_b200.so.
+ *
+ * Drop-in for the reference bridge: every declaration below keeps the name,
+ * argument order, meaning and return convention of the symbol it replaces
+ * (cited per function). Plain pointers and ints only; no Torch types. The
+ * Python binding (zipserv_asplos26_b200/runtime.py) and the reference's
+ * ctypes binding (integrations/vllm/zipserv_vllm/runtime.py:33-65) both bind
+ * exactly these symbols.
+ *
+ * Conventions shared by the GPU entry points:
+ *   - All device buffers belong to the caller and must stay alive until the
+ *     enqueued work completes. Work is enqueued on `stream` (a cudaStream_t,
+ *     NULL = legacy default stream); no host synchronisation, no device
+ *     allocation, so calls can be captured in CUDA graphs.
+ *   - Return 0 (cudaSuccess) or a cudaError_t value; on failure
+ *     zipserv_error() describes it. Contract violations, including null
+ *     pointers and device buffers not aligned to 16 bytes, return
+ *     cudaErrorInvalidValue (1). N == 0 returns 0 without launching.
+ *   - Shapes and pointers are validated, packed contents are not.
+ */
+#ifndef ZIPSERV_B200_BRIDGE_H
+#define ZIPSERV_B200_BRIDGE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZIPSERV_ABI_VERSION 2
+
+/* integrations/vllm/native/host_bridge.h:9-13. Seven independently malloc'd
+ * buffers in the order sm, rare, bitmap1, bitmap2, bitmap3, medium, global;
+ * lengths in bytes. Owned by the descriptor until zipserv_free(). */
+typedef struct Packed {
+    void* buffers[7];
+    uint64_t lengths[7];
+    int32_t m, k, max_common, max_rare, start_exp;
+} Packed;
+
+/* host_bridge.cpp:12. Thread-local description of the last failure. */
+const char* zipserv_error(void);
+
+/* host_bridge.cpp:13. Returns ZIPSERV_ABI_VERSION. */
+int zipserv_abi_version(void);
+
+/* host_bridge.cpp:14-16. Frees all seven buffers and nulls the pointers. */
+void zipserv_free(Packed* out);
+
+/* host_bridge.cpp:18-43. Packs a row-major BF16 m x k host matrix (m, k
+ * positive multiples of 64, m*k <= INT_MAX - 4096) with the most populated
+ * 7-exponent window; start_exp = uint8(base - 1). Returns 0, or -1 with the
+ * descriptor zeroed and nothing allocated. Synchronous; the input must stay
+ * unchanged during the call. Output is byte-identical to the reference. */
+int zipserv_compress(const void* weights, int m, int k, Packed* out);
+
+/* bridge.cu:8-21 (BF16TripleBitmap_MM_API). y[n, m] = sum_k W[m, k] x[n, k]
+ * with W decoded bit-exactly from the seven buffers, FP32 accumulation and
+ * BF16 output; x is [n, k] and y is [n, m], both row-major BF16.
+ * split_k keeps the reference's contract (>= 1, divides k/64, workspace of
+ * split_k*n*m BF16 elements required when split_k > 1) but the reduction over
+ * K runs inside the kernel in FP32: the workspace is validated and never
+ * written, and the kernel chooses its own K partition for the GPU. */
+int zipserv_mm(void* stream, const void* sm, const void* rare, const void* b1,
+               const void* b2, const void* b3, const void* medium, const void* global,
+               int max_common, int max_rare, int start_exp, const void* x, void* y,
+               int m, int n, int k, void* workspace, int split_k);
+
+/* bridge.cu:23-34 (BF16TripleBitmap_Decompress_API). Writes the dense
+ * row-major BF16 m x k weight, bit-exact. */
+int zipserv_decode(void* stream, const void* sm, const void* rare, const void* b1,
+                   const void* b2, const void* b3, const void* medium, const void* global,
+                   int max_common, int max_rare, int start_exp, void* output, int m, int k);
+
+/* bridge.cu:38-51 (BF16TripleBitmap_MM_API_FP32). Same as zipserv_mm with an
+ * FP32 workspace contract (split_k*n*m floats when split_k > 1); again the
+ * reduction stays in the kernel and the workspace is not written. */
+int zipserv_mm_fp32(void* stream, const void* sm, const void* rare, const void* b1,
+                    const void* b2, const void* b3, const void* medium, const void* global,
+                    int max_common, int max_rare, int start_exp, const void* x, void* y,
+                    int m, int n, int k, void* workspace, int split_k);
+
+/* ---- Extensions (no counterpart in the reference bridge) ---------------- */
+
+/* zipserv_mm with an explicit in-kernel K partition: the K tiles are split
+ * over `k_parts` CTAs of one thread-block cluster (1..16, at most k/64) whose
+ * FP32 partial sums are reduced through distributed shared memory.
+ * k_parts = 0 picks the partition for the device, as zipserv_mm does. */
+int zipserv_mm_kparts(void* stream, const void* sm, const void* rare, const void* b1,
+                      const void* b2, const void* b3, const void* medium, const void* global,
+                      int max_common, int max_rare, int start_exp, const void* x, void* y,
+                      int m, int n, int k, int k_parts);
+
+/* The K partition zipserv_mm picks for this shape on the current device, or
+ * a negative value if the shape is invalid. */
+int zipserv_mm_plan(int m, int n, int k);
+
+/* Device-side failure flags of the current device (bit 0: a pipeline wait
+ * in a kernel gave up after its iteration limit; results of that launch are
+ * undefined). Reading synchronises the device; clear != 0 resets the flags.
+ * Returns a cudaError_t. */
+int zipserv_device_flags(unsigned* flags, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
