@@ -1,0 +1,483 @@
+"""ZipGEMM benchmark: compressed-byte HBM throughput on the Llama-3-8B decode sweep.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the four Llama-3-8B linears, qkv 6144x4096,
+o 4096x4096, gate_up 28672x4096 and down 4096x14336, weights ~N(0, 0.02) BF16
+packed to TCA-TBE, activations ~N(0, 1) BF16 with N in {1, 8, 16, 32, 64, 128}
+tokens. One step = the 24 fused ZipGEMM calls (4 linears x 6 token counts).
+The metric is BASELINE's: ZipGEMM HBM GB/s on compressed bytes, i.e.
+algorithmic bytes (packed weight + activations + BF16 output) / time.
+
+Timing: every call is bracketed by CUDA events on its stream; the 256 MiB
+L2 flush that precedes each call lies outside the events, so every call reads
+its weights from HBM. value = total bytes / summed call time (max over ranks
+for N > 1). e2e repeats the step through the public API (runtime.linear) with
+the activations copied from pinned host memory and the outputs copied back
+inside the timed region. cuBLAS BF16 on the dense weights is timed the same
+way. With --gpus N (torchrun), every linear is split Megatron-style:
+qkv/gate_up by output rows (no collective), o/down by K with an NCCL
+all-reduce of the BF16 partial outputs inside the timed region.
+
+--impl reference times the reference's CPU implementation of the path (the
+restated decoder and FP32 GEMM of oracle/, all host threads) on the same
+metric: each step decodes the o-projection weight and multiplies it with 8
+tokens.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS = (  # name, M (out features), K (in features), tensor-parallel split
+    ("qkv", 6144, 4096, "col"),
+    ("o", 4096, 4096, "row"),
+    ("gate_up", 28672, 4096, "col"),
+    ("down", 4096, 14336, "row"),
+)
+TOKENS = (1, 8, 16, 32, 64, 128)
+FLUSH_BYTES = 256 * 2**20  # 2x the 126 MB L2
+METRIC = "zipgemm_hbm_gbs_compressed_llama3_8b_decode_sweep"
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_id: str | None):
+        self.device_id = device_id
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+               "-lms", "200"]
+        if self.device_id:
+            cmd += ["-i", self.device_id]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, sm_max, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(sm_max),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _pci_id(torch, dev) -> str | None:
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:
+        return None
+
+
+def _shard(name, m, k, split, world, rank):
+    if world == 1:
+        return m, k, (0, m), (0, k)
+    if split == "col":
+        mm = m // world
+        return mm, k, (rank * mm, (rank + 1) * mm), (0, k)
+    kk = k // world
+    return m, kk, (0, m), (rank * kk, (rank + 1) * kk)
+
+
+def run_ours(args, world: int, rank: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from zipserv_asplos26_b200 import runtime
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    runtime._cuda_library()  # fail loudly without the native library
+    gen = torch.Generator().manual_seed(0)
+    layers = []
+    for li, (name, m, k, split) in enumerate(LAYERS):
+        g = torch.Generator().manual_seed(1000 + li)
+        full = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16)
+        mm, kk, (r0, r1), (c0, c1) = _shard(name, m, k, split, world, rank)
+        local = full[r0:r1, c0:c1].contiguous()
+        packed = runtime.compress(local)
+        layers.append({
+            "name": name, "m": mm, "k": kk, "split": split, "full_m": m, "full_k": k,
+            "packed": packed.to(dev), "dense": local.to(dev),
+            "storage": packed.storage_bytes,
+        })
+        del full
+    xs = {}
+    for lay in layers:
+        for n in args.tokens:
+            xs[(lay["name"], n)] = torch.randn(n, lay["k"], generator=gen).to(torch.bfloat16).to(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    need_reduce = world > 1
+
+    def call_bytes(lay, n):
+        return lay["storage"] + 2 * n * lay["k"] + 2 * n * lay["m"]
+
+    calls = [(lay, n) for lay in layers for n in args.tokens]
+    total_bytes = sum(call_bytes(lay, n) for lay, n in calls)
+    outs = {(lay["name"], n): torch.empty(n, lay["m"], dtype=torch.bfloat16, device=dev)
+            for lay, n in calls}
+
+    def zip_call(lay, n):
+        y = runtime.linear_kparts(xs[(lay["name"], n)], lay["packed"], 0, out=outs[(lay["name"], n)])
+        if need_reduce and lay["split"] == "row":
+            dist.all_reduce(y)
+        return y
+
+    def dense_call(lay, n):
+        y = F.linear(xs[(lay["name"], n)], lay["dense"])
+        if need_reduce and lay["split"] == "row":
+            dist.all_reduce(y)
+        return y
+
+    def timed_step(fn, per_call: dict | None = None):
+        total = 0.0
+        events = []
+        # Keep the GPU busy while the host enqueues the step, so no timed call
+        # starts on an idle queue and absorbs host launch latency.
+        torch.cuda._sleep(4_000_000)
+        for lay, n in calls:
+            flush.zero_()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            fn(lay, n)
+            end.record(stream)
+            events.append((lay["name"], n, start, end))
+        torch.cuda.synchronize(dev)
+        for name, n, s, e in events:
+            ms = s.elapsed_time(e)
+            total += ms
+            if per_call is not None:
+                per_call.setdefault((name, n), []).append(ms)
+        return total
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # Warm-up (also primes the planner and tensor-map encoder).
+    for _ in range(args.warmup):
+        timed_step(zip_call)
+        timed_step(dense_call)
+    barrier()
+    per_call: dict = {}
+    dense_per_call: dict = {}
+    sampler = ClockSampler(_pci_id(torch, dev) if rank == 0 else None)
+    wall0 = time.time()
+    with sampler if rank == 0 else _Null():
+        barrier()
+        zip_ms = [timed_step(zip_call, per_call) for _ in range(args.steps)]
+        barrier()
+    wall = time.time() - wall0
+    dense_ms = [timed_step(dense_call, dense_per_call) for _ in range(args.steps)]
+    barrier()
+
+    # End to end through the public API: H2D of activations, GEMM, D2H of outputs.
+    host_x = {key: x.cpu().pin_memory() for key, x in xs.items()}
+    host_y = {key: torch.empty(o.shape, dtype=o.dtype).pin_memory() for key, o in outs.items()}
+    dev_x = {key: torch.empty_like(x) for key, x in xs.items()}
+    h2d = sum(x.numel() * 2 for x in host_x.values())
+    d2h = sum(y.numel() * 2 for y in host_y.values())
+
+    def e2e_call(lay, n):
+        key = (lay["name"], n)
+        dev_x[key].copy_(host_x[key], non_blocking=True)
+        y = runtime.linear(dev_x[key], lay["packed"])
+        if need_reduce and lay["split"] == "row":
+            dist.all_reduce(y)
+        host_y[key].copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        timed_step(e2e_call)
+    barrier()
+    e2e_ms = [timed_step(e2e_call) for _ in range(args.steps)]
+    barrier()
+
+    def agg(values):
+        t = torch.tensor([sum(values)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    zip_total, dense_total, e2e_total = agg(zip_ms), agg(dense_ms), agg(e2e_ms)
+    bytes_all = torch.tensor([float(total_bytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(bytes_all)
+    step_bytes = float(bytes_all.item())
+    if rank != 0:
+        return None
+    steps = args.steps
+    value = step_bytes * steps / (zip_total * 1e-3) / 1e9
+    peaks = _peaks()
+    per_shape = []
+    for lay, n in calls:
+        key = (lay["name"], n)
+        us = statistics.median(per_call[key]) * 1e3
+        dus = statistics.median(dense_per_call[key]) * 1e3
+        per_shape.append({"layer": lay["name"], "m": lay["m"], "k": lay["k"], "n": n,
+                          "zipgemm_us": round(us, 2), "cublas_bf16_us": round(dus, 2),
+                          "gbs": round(call_bytes(lay, n) / (us * 1e-6) / 1e9, 1),
+                          "speedup_vs_cublas": round(dus / us, 3)})
+    traffic = _traffic_record()
+    launches = len(calls) * steps
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(zip_total / steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": {
+            "workload": "llama3-8b linears qkv/o/gate_up/down x tokens {1,8,16,32,64,128}",
+            "tokens": list(args.tokens),
+            "split_k": "in-kernel cluster partition (auto)",
+            "l2": "256 MiB flush before every call, outside the timed events",
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "bytes_per_step": int(step_bytes),
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(value, 1),
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(value / peaks["hbm_gbs"], 4),
+            "peak_source": peaks["source"],
+            "traffic": traffic.get("traffic_bytes_per_launch"),
+            "traffic_note": traffic.get("note"),
+        },
+        "cublas_bf16": {
+            "ms_per_step": round(dense_total / steps, 4),
+            "zipgemm_speedup": round(dense_total / zip_total, 3),
+        },
+        "e2e": {
+            "value": round(step_bytes * steps / (e2e_total * 1e-3) / 1e9, 1),
+            "unit": "GB/s",
+            "ms_per_step": round(e2e_total / steps, 4),
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+        },
+        "gpu_launches": launches,
+        "wall_s_timed_region": round(wall, 3),
+        "per_shape": per_shape,
+    }
+    line["clocks"] = sampler.summary()
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args)
+    return line
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+def _traffic_record() -> dict:
+    path = ROOT / "profiles" / "zipgemm_traffic.json"
+    if path.is_file():
+        return json.loads(path.read_text())
+    return {"traffic_bytes_per_launch": None, "note": "no ncu capture recorded"}
+
+
+def _cpu_case(name: str, n: int, threads: int):
+    """Decode one Llama-3-8B linear on the host and multiply it with n tokens."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle
+
+    spec = {lay[0]: lay for lay in LAYERS}[name]
+    _, m, k, _ = spec
+    g = torch.Generator().manual_seed(1000 + [lay[0] for lay in LAYERS].index(name))
+    w = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    packed = oracle.pack(w)
+    x = torch.randn(n, k, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
+    xw = x.view(torch.int16).numpy().view(np.uint16)
+    storage = sum(b.nbytes for b in packed.abi_buffers())
+
+    def run():
+        dec = oracle.decode(packed.abi_buffers(), m, k, packed.start_exp, threads=threads)
+        oracle.gemm(dec, xw, threads=threads)
+
+    return run, storage + 2 * n * k + 2 * n * m
+
+
+def cpu_baseline(args) -> dict:
+    threads = os.cpu_count() or 1
+    run, nbytes = _cpu_case("o", 8, threads)
+    run()
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 3 or time.perf_counter() - t0 < 10.0:
+        run()
+        reps += 1
+        if time.perf_counter() - t0 > 30.0:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(nbytes * reps / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"o-proj 4096x4096 decode + FP32 GEMM with 8 tokens, {reps} repetitions "
+                      f"({dt:.1f} s), oracle/ restatement of the reference CPU decoder and GEMM"}
+
+
+def run_reference(args, world: int, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    run, nbytes = _cpu_case("o", 8, threads)
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = nbytes * len(times) / total / 1e9
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "llama3-8b o-proj 4096x4096, 8 tokens (bounded CPU sample of the "
+                               "decode sweep)", "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": "per step: decode the packed o-proj weight and an FP32 GEMM "
+                                   "with 8 tokens (oracle/ restatement of the reference CPU path)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def run_profile_case(spec: str, repeats: int) -> None:
+    """Run one linear `repeats` times (for ncu captures; prints nothing timed)."""
+    import torch
+
+    from zipserv_asplos26_b200 import runtime
+
+    name, n = spec.split(":")
+    n = int(n)
+    lay = {l[0]: l for l in LAYERS}[name]
+    _, m, k, _ = lay
+    g = torch.Generator().manual_seed(1000 + [l[0] for l in LAYERS].index(name))
+    w = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16)
+    packed = runtime.compress(w).to("cuda")
+    x = torch.randn(n, k, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).cuda()
+    for _ in range(repeats):
+        runtime.linear(x, packed)
+    torch.cuda.synchronize()
+    if runtime.device_flags() != 0:
+        raise SystemExit("device wait timeout flag set")
+    print(json.dumps({"profile_case": spec, "m": m, "k": k, "n": n, "repeats": repeats,
+                      "algorithmic_bytes_per_launch": packed.storage_bytes + 2 * n * k + 2 * n * m,
+                      "kparts": runtime.plan_kparts(m, n, k)}))
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--tokens", type=int, nargs="*", default=list(TOKENS))
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile", metavar="LAYER:N", help="run one linear for ncu, e.g. o:16")
+    parser.add_argument("--repeats", type=int, default=4)
+    args = parser.parse_args()
+    if args.profile:
+        run_profile_case(args.profile, args.repeats)
+        return
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        line = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

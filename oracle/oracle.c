@@ -170,47 +170,98 @@ int oracle_pack(const uint16_t* words, int m, int k, int base, int include_small
     return 0;
 }
 
-int oracle_decode(const uint8_t* sm, const uint16_t* rare, const uint64_t* b1,
-                  const uint64_t* b2, const uint64_t* b3, const int32_t* medium,
-                  const int32_t* global, int m, int k, int start_exp, uint16_t* out) {
+typedef struct decode_job {
+    const uint8_t* sm;
+    const uint16_t* rare;
+    const uint64_t *b1, *b2, *b3;
+    const int32_t *medium, *global;
+    int m, k, start_exp, t0, t1;
+    uint16_t* out;
+    int status;
+} decode_job;
+
+static int decode_tiles(const decode_job* j) {
     /* tests/test_host_packer.cpp:14-44: invert the small-tile index
      * row = 64*(t/kt) + 16*(s/16) + 8*(s%2), col = 64*(t%kt) + 16*((s/4)%4) + 8*((s/2)%2). */
-    const int kt = k / 64;
-    const int tiles = (m / 64) * kt;
-    const uint64_t total_common = (uint64_t)global[2 * tiles];
-    const uint64_t total_rare = (uint64_t)global[2 * tiles + 1];
-    for (int t = 0; t < tiles; ++t) {
-        int64_t ci = global[2 * t], ri = global[2 * t + 1];
+    const int kt = j->k / 64;
+    const int tiles = (j->m / 64) * kt;
+    const uint64_t total_common = (uint64_t)j->global[2 * tiles];
+    const uint64_t total_rare = (uint64_t)j->global[2 * tiles + 1];
+    for (int t = j->t0; t < j->t1; ++t) {
+        int64_t ci = j->global[2 * t], ri = j->global[2 * t + 1];
         for (int s = 0; s < 64; ++s) {
             if (s % 16 == 0) {
-                if (medium[t * 8 + (s / 16) * 2] != ci - global[2 * t]) return 1;
-                if (medium[t * 8 + (s / 16) * 2 + 1] != ri - global[2 * t + 1]) return 1;
+                if (j->medium[t * 8 + (s / 16) * 2] != ci - j->global[2 * t]) return 1;
+                if (j->medium[t * 8 + (s / 16) * 2 + 1] != ri - j->global[2 * t + 1]) return 1;
             }
             const int row = (t / kt) * 64 + (s / 16) * 16 + (s % 2) * 8;
             const int col = (t % kt) * 64 + ((s / 4) % 4) * 16 + ((s / 2) % 2) * 8;
             const size_t small = (size_t)t * 64 + s;
             for (int bit = 0; bit < 64; ++bit) {
-                const unsigned code = (unsigned)((b1[small] >> bit) & 1u) |
-                                      (unsigned)(((b2[small] >> bit) & 1u) << 1) |
-                                      (unsigned)(((b3[small] >> bit) & 1u) << 2);
+                const unsigned code = (unsigned)((j->b1[small] >> bit) & 1u) |
+                                      (unsigned)(((j->b2[small] >> bit) & 1u) << 1) |
+                                      (unsigned)(((j->b3[small] >> bit) & 1u) << 2);
                 uint16_t w;
                 if (code) {
                     if ((uint64_t)ci >= total_common) return 3;
-                    const uint8_t p = sm[ci++];
+                    const uint8_t p = j->sm[ci++];
                     w = (uint16_t)(((p & 128u) << 8) |
-                                   oracle_exponent_bits((uint8_t)start_exp, (uint8_t)code) |
+                                   oracle_exponent_bits((uint8_t)j->start_exp, (uint8_t)code) |
                                    (p & 127u));
                 } else {
                     if ((uint64_t)ri >= total_rare) return 3;
-                    w = rare[ri++];
+                    w = j->rare[ri++];
                 }
-                out[(size_t)(row + bit / 8) * k + col + bit % 8] = w;
+                j->out[(size_t)(row + bit / 8) * j->k + col + bit % 8] = w;
             }
         }
-        if ((ci + 15) / 16 * 16 != global[2 * (t + 1)]) return 2;
-        if ((ri + 7) / 8 * 8 != global[2 * (t + 1) + 1]) return 2;
+        if ((ci + 15) / 16 * 16 != j->global[2 * (t + 1)]) return 2;
+        if ((ri + 7) / 8 * 8 != j->global[2 * (t + 1) + 1]) return 2;
     }
     return 0;
+}
+
+static void* decode_thread(void* arg) {
+    decode_job* j = (decode_job*)arg;
+    j->status = decode_tiles(j);
+    return NULL;
+}
+
+int oracle_decode_mt(const uint8_t* sm, const uint16_t* rare, const uint64_t* b1,
+                     const uint64_t* b2, const uint64_t* b3, const int32_t* medium,
+                     const int32_t* global, int m, int k, int start_exp, uint16_t* out,
+                     int threads) {
+    const int tiles = (m / 64) * (k / 64);
+    if (threads < 1) threads = 1;
+    if (threads > tiles) threads = tiles;
+    decode_job* jobs = (decode_job*)xmalloc(sizeof(decode_job) * (size_t)threads);
+    pthread_t* ids = (pthread_t*)xmalloc(sizeof(pthread_t) * (size_t)threads);
+    int* started = (int*)xmalloc(sizeof(int) * (size_t)threads);
+    for (int i = 0; i < threads; ++i) {
+        decode_job j = {sm, rare, b1, b2, b3, medium, global, m, k, start_exp,
+                        (int)((int64_t)tiles * i / threads), (int)((int64_t)tiles * (i + 1) / threads),
+                        out, 0};
+        jobs[i] = j;
+        started[i] = 0;
+    }
+    for (int i = 1; i < threads; ++i) started[i] = pthread_create(&ids[i], NULL, decode_thread, &jobs[i]) == 0;
+    jobs[0].status = decode_tiles(&jobs[0]);
+    int status = jobs[0].status;
+    for (int i = 1; i < threads; ++i) {
+        if (started[i]) pthread_join(ids[i], NULL);
+        else jobs[i].status = decode_tiles(&jobs[i]);
+        if (!status) status = jobs[i].status;
+    }
+    free(jobs);
+    free(ids);
+    free(started);
+    return status;
+}
+
+int oracle_decode(const uint8_t* sm, const uint16_t* rare, const uint64_t* b1,
+                  const uint64_t* b2, const uint64_t* b3, const int32_t* medium,
+                  const int32_t* global, int m, int k, int start_exp, uint16_t* out) {
+    return oracle_decode_mt(sm, rare, b1, b2, b3, medium, global, m, k, start_exp, out, 1);
 }
 
 uint16_t oracle_f32_to_bf16(float value) {

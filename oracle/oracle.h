@@ -64,6 +64,13 @@ int oracle_decode(const uint8_t* sm, const uint16_t* rare, const uint64_t* b1,
                   const uint64_t* b2, const uint64_t* b3, const int32_t* medium,
                   const int32_t* global, int m, int k, int start_exp, uint16_t* out);
 
+/* oracle_decode split over `threads` host threads by tile ranges (each tile
+ * is independent given the global offsets); same result. */
+int oracle_decode_mt(const uint8_t* sm, const uint16_t* rare, const uint64_t* b1,
+                     const uint64_t* b2, const uint64_t* b3, const int32_t* medium,
+                     const int32_t* global, int m, int k, int start_exp, uint16_t* out,
+                     int threads);
+
 /* Round-to-nearest-even FP32 -> BF16, as __float2bfloat16_rn. */
 uint16_t oracle_f32_to_bf16(float value);
 float oracle_bf16_to_f32(uint16_t bits);

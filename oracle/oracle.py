@@ -65,6 +65,7 @@ def lib() -> ctypes.CDLL:
         l.oracle_free.argtypes = [ctypes.POINTER(_Packed)]
         l.oracle_decode.argtypes = [_u8p, _u16p, _u64p, _u64p, _u64p, _i32p, _i32p,
                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p]
+        l.oracle_decode_mt.argtypes = l.oracle_decode.argtypes + [ctypes.c_int]
         l.oracle_gemm.argtypes = [_u16p, _u16p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   _u16p, _f32p, ctypes.c_int]
         l.oracle_gemm.restype = None
@@ -150,17 +151,17 @@ def pack(words: np.ndarray, base: int = -1, include_small: bool = False) -> Orac
         lib().oracle_free(ctypes.byref(out))
 
 
-def decode(buffers, m: int, k: int, start_exp: int) -> np.ndarray:
+def decode(buffers, m: int, k: int, start_exp: int, threads: int = 1) -> np.ndarray:
     """Bit-exact CPU decode of the seven ABI buffers; raises on inconsistency."""
     sm, rare, b1, b2, b3, medium, glob = (np.ascontiguousarray(b).view(np.uint8) for b in buffers)
     out = np.empty((m, k), dtype=np.uint16)
     sm = sm if sm.size else np.zeros(16, np.uint8)
     rare = rare if rare.size else np.zeros(16, np.uint8)
-    status = lib().oracle_decode(
+    status = lib().oracle_decode_mt(
         _ptr(sm, _u8p), _ptr(rare.view(np.uint16), _u16p), _ptr(b1.view(np.uint64), _u64p),
         _ptr(b2.view(np.uint64), _u64p), _ptr(b3.view(np.uint64), _u64p),
         _ptr(medium.view(np.int32), _i32p), _ptr(glob.view(np.int32), _i32p),
-        m, k, start_exp, _ptr(out, _u16p))
+        m, k, start_exp, _ptr(out, _u16p), threads)
     if status:
         raise ValueError(f"packed buffers are inconsistent (oracle code {status})")
     return out
