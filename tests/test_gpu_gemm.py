@@ -192,3 +192,43 @@ def test_cuda_graph_capture_and_streams(native_lib, oracle_mod):
     graph.replay()
     torch.cuda.synchronize()
     assert np.array_equal(words_of(y), expected)
+
+
+def scattered(packed: runtime.PackedWeight) -> runtime.PackedWeight:
+    """The same streams at unequal distances (bitmap planes not equally
+    spaced), so the kernels take their per-plane copy path."""
+    sizes = [b.numel() for b in packed.buffers]
+    offsets, total = [], 0
+    for i, size in enumerate(sizes):
+        offsets.append(total)
+        total += (size + 255) // 256 * 256 + 256 * (i + 1)
+    storage = torch.zeros(total, dtype=torch.uint8, device="cuda")
+    views = []
+    for b, off in zip(packed.buffers, offsets):
+        v = storage[off:off + b.numel()]
+        v.copy_(b)
+        views.append(v)
+    return runtime.PackedWeight(tuple(views), packed.m, packed.k, packed.max_common,
+                                packed.max_rare, packed.start_exp)
+
+
+@pytest.mark.parametrize("m,k", [(192, 640), (64, 64), (320, 2112)])
+def test_unequally_spaced_bitmaps(native_lib, oracle_mod, m, k):
+    rng = oracle_mod.MT19937(m + k)
+    w = oracle_mod.integer_matrix(rng, m * k).reshape(m, k)
+    cpu = runtime.compress(bf16_tensor(w))
+    packed = scattered(cpu)
+    planes = [b.data_ptr() for b in packed.buffers[2:5]]
+    assert planes[1] - planes[0] != planes[2] - planes[1]
+    for n in (1, 17, 64):
+        x = oracle_mod.integer_matrix(rng, n * k).reshape(n, k)
+        expected, _ = oracle_mod.gemm(w, x)
+        x_dev = bf16_tensor(x).cuda()
+        for kparts in sorted({1, min(3, k // 64)}):
+            y = runtime.linear_kparts(x_dev, packed, kparts)
+            torch.cuda.synchronize()
+            assert np.array_equal(words_of(y), expected), (n, kparts)
+    dense = runtime.decompress(packed)
+    torch.cuda.synchronize()
+    assert np.array_equal(words_of(dense), w)
+    assert runtime.device_flags() == 0

@@ -3,8 +3,8 @@
 //
 // Persistent grid, one CTA per SM. The CTA walks chunks of 2*half
 // consecutive global tiles (row-major tile order) with stride gridDim.x; the
-// packed streams of a chunk are contiguous, so each half of it arrives with
-// six bulk copies whatever its length. Warp roles:
+// packed streams of a chunk are contiguous, so a chunk arrives with five
+// copies whatever its length. Warp roles:
 //   warp 0     producer: bulk async copies of each chunk's bitmaps, band
 //              offsets and payloads into a ring of shared-memory slots;
 //   warps 1..8 two decoder groups (four warps each, one chunk per group at
@@ -40,7 +40,8 @@ constexpr int kDecStages = 8;  // ring slots at most; fewer when payload capacit
 constexpr uint32_t kOutTileBytes = 32 * 128;  // one warp's 32 rows x 64 BF16
 
 __global__ void __launch_bounds__(kDecThreads, 1)
-    decompress_kernel(const __grid_constant__ CUtensorMap omap, const DecompressParams p) {
+    decompress_kernel(const __grid_constant__ CUtensorMap omap,
+                      const __grid_constant__ PlaneMaps pm, const DecompressParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = ptx::smem_addr(smem);
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const uint32_t tables = sbase + kBarrierBytes;
     const uint32_t cap_c = p.cap_c, cap_r = p.cap_r;
     const int H = p.half, C = 2 * p.half;
-    const uint32_t pstride = 512u * uint32_t(H);
+    const SlotLayout L = p.slot;
     const int nlocal = p.chunks > int(blockIdx.x)
                            ? (p.chunks - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x)
                            : 0;
@@ -65,15 +66,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     __syncthreads();
     if (tid == 0) {
         ptx::prefetch_tensormap(&omap);
+        for (int i = 0; i < pm.count; ++i) ptx::prefetch_tensormap(&pm.map[i]);
         ptx::mbar_arrive_expect_tx(bar_tab, kTableBytes);
         ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
     }
 
     if (warp == 0) {
         // ------------------------------------------------------ producer
+        // Per chunk: one tensor load for the bitmap planes (tiles past the end
+        // arrive zero-filled), one bulk copy of the band offsets, one of each
+        // half's common payload and one of the chunk's rare payload.
         const uint64_t pol = ptx::policy_evict_first();
         const int2* goffs = reinterpret_cast<const int2*>(p.global);
-        // Lane i holds offset entry i (tiles t0 + i, i <= C) of the chunk in
+        const uint32_t plane_bytes = 3u * 512u * uint32_t(C);
+        // Lane i holds offset entry i (tile t0 + i, i <= C) of the chunk in
         // flight; the next chunk's entries are loaded one iteration early.
         auto load = [&](int it) {
             const int t = (int(blockIdx.x) + it * int(gridDim.x)) * C + lane;
@@ -91,65 +97,49 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             ok = __shfl_sync(kFullMask, ok, 0) != 0;
             if (!ok) break;
             const int t0 = (int(blockIdx.x) + it * int(gridDim.x)) * C;
-            const uint32_t slot = sbase + p.off_slots + uint32_t(s) * p.slot.bytes;
+            const uint32_t slot = sbase + p.off_slots + uint32_t(s) * L.bytes;
             const uint32_t full = bar_full + 8 * s;
-            int nt[2];
-            nt[0] = min(H, p.tiles - t0);
-            nt[1] = max(0, min(H, p.tiles - t0 - H));
-            uint32_t clen[2] = {0, 0}, rlen[2] = {0, 0};
-            int2 g0[2];
-            uint32_t bytes = 0;
-            for (int tau = 0; tau < 2; ++tau) {
-                g0[tau].x = __shfl_sync(kFullMask, cur.x, tau * H);
-                g0[tau].y = __shfl_sync(kFullMask, cur.y, tau * H);
-                const int ex = __shfl_sync(kFullMask, cur.x, tau * H + nt[tau]);
-                const int ey = __shfl_sync(kFullMask, cur.y, tau * H + nt[tau]);
-                // Payload copies need 16-byte aligned sources; offsets of
-                // valid packed data always are.
-                if (nt[tau] && (g0[tau].x & 15) == 0)
-                    clen[tau] = min(uint32_t(max(ex - g0[tau].x, 0)), uint32_t(H) * cap_c) & ~15u;
-                if (nt[tau] && (g0[tau].y & 7) == 0)
-                    rlen[tau] =
-                        (min(uint32_t(max(ey - g0[tau].y, 0)), uint32_t(H) * cap_r) * 2u) & ~15u;
-                bytes += 3u * 512u * uint32_t(nt[tau]) + 32u * uint32_t(nt[tau]) + clen[tau] +
-                         rlen[tau];
-            }
-            // Per-tile payload starts relative to the half's run, clamped so
-            // tile i reads inside its region whatever the offsets say; tiles
-            // missing at the end of the matrix get zero starts.
+            const int n = min(C, p.tiles - t0);  // tiles in this chunk
+            const int nt0 = min(H, n), nt1 = n - nt0;
+            int2 st[2], en[2];
+            st[0].x = __shfl_sync(kFullMask, cur.x, 0), st[0].y = __shfl_sync(kFullMask, cur.y, 0);
+            en[0].x = __shfl_sync(kFullMask, cur.x, nt0);
+            st[1].x = en[0].x;
+            en[1].x = __shfl_sync(kFullMask, cur.x, n);
+            en[1].y = __shfl_sync(kFullMask, cur.y, n);
+            // Payload copies need 16-byte aligned sources; offsets of valid
+            // packed data always are.
+            const uint32_t clen0 =
+                (st[0].x & 15) == 0 ? min(uint32_t(max(en[0].x - st[0].x, 0)), uint32_t(H) * cap_c) & ~15u : 0u;
+            const uint32_t clen1 = nt1 && (st[1].x & 15) == 0
+                                       ? min(uint32_t(max(en[1].x - st[1].x, 0)), uint32_t(H) * cap_c) & ~15u
+                                       : 0u;
+            const uint32_t rlen =
+                (st[0].y & 7) == 0
+                    ? (min(uint32_t(max(en[1].y - st[0].y, 0)), uint32_t(C) * cap_r) * 2u) & ~15u
+                    : 0u;
+            // Per-tile payload starts (common: within its half's run; rare:
+            // within the chunk's run), clamped so tile i reads inside its
+            // region whatever the offsets say; missing tiles get zero starts.
             if (lane < C) {
                 const int tau = lane >= H, i = lane - tau * H;
                 int2 h = make_int2(0, 0);
-                if (i < nt[tau])
-                    h = make_int2(min(max(cur.x - g0[tau].x, 0), int(uint32_t(i) * cap_c)),
-                                  min(max(cur.y - g0[tau].y, 0), int(uint32_t(i) * cap_r)));
-                reinterpret_cast<int2*>(smem + p.off_slots + uint32_t(s) * p.slot.bytes +
-                                        p.slot.hdr)[tau * kMaxGroup + i] = h;
+                if (lane < n)
+                    h = make_int2(min(max(cur.x - st[tau].x, 0), int(uint32_t(i) * cap_c)),
+                                  min(max(cur.y - st[0].y, 0), int(uint32_t(lane) * cap_r)));
+                reinterpret_cast<int2*>(smem + p.off_slots + uint32_t(s) * L.bytes +
+                                        L.hdr)[tau * kMaxGroup + i] = h;
             }
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive_expect_tx(full, bytes);
+            if (lane == 0)
+                ptx::mbar_arrive_expect_tx(full, plane_bytes + 32u * uint32_t(n) + clen0 + clen1 + rlen);
             __syncwarp();
-            if (lane < 12) {
-                const int tau = lane / 6, c = lane % 6;
-                const size_t t = size_t(t0 + tau * H);
-                if (nt[tau]) {
-                    if (c < 3) {
-                        const uint64_t* src = c == 0 ? p.b1 : c == 1 ? p.b2 : p.b3;
-                        ptx::bulk_g2s(slot + (tau ? p.slot.plane1 : 0u) + uint32_t(c) * pstride,
-                                      src + t * 64, 512u * uint32_t(nt[tau]), full, pol);
-                    } else if (c == 3) {
-                        ptx::bulk_g2s(slot + p.slot.med + uint32_t(tau) * 32u * H, p.medium + t * 8,
-                                      32u * uint32_t(nt[tau]), full, pol);
-                    } else if (c == 4) {
-                        if (clen[tau])
-                            ptx::bulk_g2s(slot + (tau ? p.slot.common1 : p.slot.common0),
-                                          p.sm + g0[tau].x, clen[tau], full, pol);
-                    } else if (rlen[tau]) {
-                        ptx::bulk_g2s(slot + (tau ? p.slot.rare1 : p.slot.rare0), p.rare + g0[tau].y,
-                                      rlen[tau], full, pol);
-                    }
-                }
-            }
+            ptx::load_planes(slot, L.plane_stride, pm.map, pm.count, t0, 0, full, pol, lane);
+            if (lane == 3)
+                ptx::bulk_g2s(slot + L.med, p.medium + size_t(t0) * 8, 32u * uint32_t(n), full, pol);
+            if (lane == 4 && clen0) ptx::bulk_g2s(slot + L.common0, p.sm + st[0].x, clen0, full, pol);
+            if (lane == 5 && clen1) ptx::bulk_g2s(slot + L.common1, p.sm + st[1].x, clen1, full, pol);
+            if (lane == 6 && rlen) ptx::bulk_g2s(slot + L.rare0, p.rare + st[0].y, rlen, full, pol);
             ++issued;
         }
         if (lane == 0)
@@ -174,15 +164,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (!__all_sync(kFullMask, ok)) break;
             const int t0 = (int(blockIdx.x) + it * int(gridDim.x)) * C;
             const int n0 = min(H, p.tiles - t0), n1 = max(0, min(H, p.tiles - t0 - H));
-            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(s) * p.slot.bytes);
-            const uint32_t plane = slot + (tau ? p.slot.plane1 : 0u);
-            const uint32_t med = slot + p.slot.med + uint32_t(tau) * 32u * H;
-            const uint32_t com = slot + (tau ? p.slot.common1 : p.slot.common0);
-            const uint32_t rar = slot + (tau ? p.slot.rare1 : p.slot.rare0);
+            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(s) * L.bytes);
+            const uint32_t plane = slot + uint32_t(tau) * L.plane1;
+            const uint32_t med = slot + L.med + uint32_t(tau * H) * 32u;
+            const uint32_t com = slot + (tau ? L.common1 : L.common0);
             for (int j = 0; j < n0; ++j) {
-                const int2 hdr = ptx::lds_s64(slot + p.slot.hdr + uint32_t(tau * kMaxGroup + j) * 8u);
-                dec.decode(plane + 512u * uint32_t(j), pstride, med + 32u * uint32_t(j),
-                           com + uint32_t(hdr.x), rar + 2u * uint32_t(hdr.y), cap_c, cap_r, out);
+                const int2 hdr = ptx::lds_s64(slot + L.hdr + uint32_t(tau * kMaxGroup + j) * 8u);
+                dec.decode(plane + 512u * uint32_t(j), L.plane_stride, med + 32u * uint32_t(j),
+                           com + uint32_t(hdr.x), slot + L.rare0 + 2u * uint32_t(hdr.y), cap_c,
+                           cap_r, out);
                 // Stage the warp's 32 rows: row `lane`, 16-byte chunk c at
                 // position c ^ (row & 7) (the TMA 128-byte swizzle).
                 const uint32_t buf = obuf + uint32_t(nstore & 1) * kOutTileBytes;
@@ -230,9 +220,6 @@ cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* r
     DecompressParams p{};
     p.sm = static_cast<const uint8_t*>(sm);
     p.rare = static_cast<const uint16_t*>(rare);
-    p.b1 = static_cast<const uint64_t*>(b1);
-    p.b2 = static_cast<const uint64_t*>(b2);
-    p.b3 = static_cast<const uint64_t*>(b3);
     p.medium = static_cast<const int*>(medium);
     p.global = static_cast<const int*>(global);
     p.m = m, p.k = k, p.kt = k / 64;
@@ -251,7 +238,7 @@ cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* r
     p.nstages = 0;
     for (int min_slots : {4, 2}) {
         for (int half : {4, 2, 1}) {
-            const SlotLayout l = slot_layout(half, p.cap_c, p.cap_r);
+            const SlotLayout l = decompress_slot_layout(half, p.cap_c, p.cap_r);
             const int n = std::min<int>(kDecStages, int(avail / l.bytes)) / kDecGroups * kDecGroups;
             if (n >= min_slots) {
                 p.half = half, p.slot = l, p.nstages = n;
@@ -283,9 +270,15 @@ cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* r
         zs_set_error("decompress: output tensor map rejected (output must be 16-byte aligned)");
         return cudaErrorInvalidValue;
     }
+    PlaneMaps pm;
+    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(p.tiles), 1, 64, uint32_t(2 * p.half), 1)) {
+        zs_set_error("decompress: bitmap tensor maps rejected (bitmaps must be 16-byte aligned)");
+        return cudaErrorInvalidValue;
+    }
+    p.plane_maps = pm.count;
     const int sms = device_sm_count(device);
     const int grid = std::max(1, std::min(p.chunks, sms));
-    decompress_kernel<<<grid, kDecThreads, total, stream>>>(omap, p);
+    decompress_kernel<<<grid, kDecThreads, total, stream>>>(omap, pm, p);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
         char msg[200];

@@ -80,6 +80,18 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
 }
+// 16-byte asynchronous copy global -> shared through L1-bypassing loads
+// (both addresses 16-byte aligned). Completion is tracked per thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst),
+                 "l"(src), "l"(policy)
+                 : "memory");
+}
+// Arrive on `bar` once all of this thread's earlier cp.async copies have
+// landed; the arrival counts toward the barrier's expected count.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -107,6 +119,27 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(policy)
         : "memory");
+}
+// 4-D tiled tensor load (no multicast), completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            int z, int w, uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar),
+        "l"(policy)
+        : "memory");
+}
+// Bitmap planes of a slot: one 4-D load when one map spans the three planes,
+// else one 3-D load per plane map (plane b lands at dst + b * plane_stride).
+__device__ __forceinline__ void load_planes(uint32_t dst, uint32_t plane_stride,
+                                            const CUtensorMap* maps, int count, int x, int y,
+                                            uint32_t bar, uint64_t policy, int lane) {
+    if (count == 1) {
+        if (lane == 0) tma_load_4d(dst, &maps[0], 0, x, y, 0, bar, policy);
+    } else if (lane < 3) {
+        tma_load_3d(dst + uint32_t(lane) * plane_stride, &maps[lane], 0, x, y, bar, policy);
+    }
 }
 // 2-D tiled tensor store from this CTA's shared memory.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, uint32_t src) {

@@ -4,25 +4,24 @@
 //
 // One CTA computes a 128-row block of W (two vertically adjacent 64x64 global
 // tiles) against a tile of up to 256 tokens over a contiguous range of 64-wide
-// K slices. The K slices stream through a ring of shared-memory slots, each
-// holding `group` consecutive slices: for consecutive tiles of one tile row
-// every stream (bitmap planes, band offsets, common and rare payloads) is
-// contiguous in global memory, so a slot takes one bulk copy per stream and
-// tile row plus one 3-D TMA load of the x tiles - 13 copies per slot instead
-// of 12 per slice (a copy costs about 100 cycles to issue, whatever its size).
-// Warp roles (1 CTA per SM):
-//   warp 0      producer: issues a slot's copies from several lanes, all
-//               completing on the slot's mbarrier;
-//   warp 1      allocates tensor memory and issues tcgen05.mma (one thread):
-//               A = decoded W slice read from TMEM, B = x tile from shared
-//               memory (128-byte swizzle), D = FP32 accumulator in TMEM;
-//   warps 2..   NDG decoder groups of four warps; group g decodes slots g,
-//               g+NDG, ... Warp w serves TMEM lanes 32*(w%4).. and decodes
-//               16-row band w%4 of both tiles (row = tile*64 + 16*band + i,
-//               TMEM lane = 32*band + 16*tile + i). Each thread rebuilds one W
-//               row (64 BF16) per slice and stores it with tcgen05.st into one
-//               of the group's TMEM A buffers, so decoded weights never touch
-//               shared memory.
+// K slices. Warp roles (1 CTA per SM):
+//   warp 0      allocates tensor memory; lane 0 issues tcgen05.mma
+//               (A = decoded W slice read from TMEM, B = x tile from shared
+//               memory, 128-byte swizzle, D = FP32 accumulator in TMEM);
+//   last warp   keeps an x ring of nx slices filled with 3-D TMA loads;
+//   warps 1..   NDG decoder groups of four warps. Group g decodes K slices
+//               g, g+NDG, ... from two compressed slots it owns: while it
+//               decodes one, the other is filling. The group issues its own
+//               copies (one 4-D tensor load for the three bitmap planes of
+//               both tile rows, one 3-D load for the band offsets, one bulk
+//               copy per payload run), lane 0 of each of its warps taking a
+//               share: an SM's copy engine takes ~100 cycles per copy, so
+//               copies are few, large and issued from four sub-partitions.
+//               Warp w decodes 16-row band w%4 of both tiles (row = tile*64 +
+//               16*band + i, TMEM lane = 32*band + 16*tile + i); each thread
+//               rebuilds one W row (64 BF16) per slice and stores it with
+//               tcgen05.st into one of the group's TMEM A buffers, so decoded
+//               weights never touch shared memory.
 // Split-K: the CTAs of a thread-block cluster (1..16) share one row block and
 // split its K slices. Each writes its FP32 accumulator tile to its own shared
 // memory; after a cluster barrier every CTA reduces a disjoint part of the
@@ -63,54 +62,49 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
     return base + 8u * uint32_t(index);
 }
 
-// Cache the (common, rare) offsets of `cnt` consecutive tiles of both tile
-// rows, starting at K slice `kt`, in shared memory ([2][kOffsetChunk + 1]).
-__device__ __forceinline__ void fetch_offsets(int2* goff, const int* global, int tr0, bool has1,
-                                              int kt_total, int kt, int cnt, int lane) {
-    for (int e = lane; e < 2 * cnt; e += 32) {
-        const int tr = e / cnt, i = e % cnt;
-        int2 v = make_int2(0, 0);
-        if (tr == 0 || has1)
-            v = reinterpret_cast<const int2*>(global)[size_t(tr0 + tr) * kt_total + kt + i];
-        goff[tr * (kOffsetChunk + 1) + i] = v;
-    }
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("barrier.cta.sync.aligned %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// NDG decoder groups. The ring size is a multiple of NDG so each group owns
-// the slots it consumes (slot = stage % ring) and its A buffers, and never
-// waits on a barrier more than one phase ahead of what it observed.
+// Warp roles: warp 0 allocates TMEM and its lane 0 issues the MMAs; warps
+// 1 .. 4*NDG form NDG decoder groups; the last warp keeps the x ring filled. Group g decodes K slices
+// g, g + NDG, ... and owns two compressed slots: while it decodes slice u
+// from one, the other is being filled with its next slice. A group issues
+// its own copies after a group barrier (no dedicated producer warp), lane 0
+// of each of its four warps taking a share, so copy issue is spread over the
+// four SM sub-partitions.
 template <int NDG>
 __global__ void __launch_bounds__(64 + 128 * NDG, 1)
-    zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const GemmParams p) {
+    zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ PlaneMaps pm,
+                   const __grid_constant__ CUtensorMap mmap, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = ptx::smem_addr(smem);
-    const uint32_t bar_full = sbase;
-    const uint32_t bar_empty = sbase + 8 * kMaxStages;
-    const uint32_t bar_afull = sbase + 16 * kMaxStages;
+    const uint32_t bar_full = sbase;                         // [2 * NDG]
+    const uint32_t bar_afull = sbase + 8 * kMaxStages;        // [kMaxABuffers]
     const uint32_t bar_aempty = bar_afull + 8 * kMaxABuffers;
-    const uint32_t bar_d = bar_aempty + 8 * kMaxABuffers;
+    const uint32_t bar_xfull = bar_aempty + 8 * kMaxABuffers;  // [kMaxX]
+    const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
+    const uint32_t bar_d = bar_xempty + 8 * kMaxX;
     const uint32_t bar_tab = bar_d + 8;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_tab - sbase) + 8);
     const uint32_t tables = sbase + kBarrierBytes;
 
     const int S = p.kparts;
-    const int G = p.group;
     const int rank = int(blockIdx.x) % S;  // == %cluster_ctarank: clusters span S consecutive x
     const int mblk = int(blockIdx.x) / S, nblk = int(blockIdx.y);
     const int kt0 = int(int64_t(p.kt) * rank / S), kt1 = int(int64_t(p.kt) * (rank + 1) / S);
     const int nk = kt1 - kt0;
-    const int nsup = (nk + G - 1) / G;  // slots this CTA streams
     const int tr0 = 2 * mblk;
     const bool has1 = tr0 + 1 < p.row_tiles;
     const uint32_t cap_c = p.cap_c, cap_r = p.cap_r;
-    const uint32_t pstride = 512u * uint32_t(G);
-    int2* goff = reinterpret_cast<int2*>(smem + p.off_goff);
+    const SlotLayout L = p.slot;
 
     if (tid == 0) {
-        for (int s = 0; s < kMaxStages; ++s) {
-            ptx::mbar_init(bar_addr(bar_full, s), 1);
-            ptx::mbar_init(bar_addr(bar_empty, s), 4 + 1);  // one decoder group + MMA commit
+        for (int s = 0; s < 2 * NDG; ++s) ptx::mbar_init(bar_addr(bar_full, s), 1);
+        for (int i = 0; i < kMaxX; ++i) {
+            ptx::mbar_init(bar_addr(bar_xfull, i), 1);
+            ptx::mbar_init(bar_addr(bar_xempty, i), 1);
         }
         for (int i = 0; i < kMaxABuffers; ++i) {
             ptx::mbar_init(bar_addr(bar_afull, i), 4);
@@ -120,10 +114,7 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
         ptx::mbar_init(bar_tab, 1);
         ptx::fence_mbar_init();
     }
-    // The first chunk of tile offsets is fetched right away, so its latency
-    // overlaps the rest of the set-up.
-    if (warp == 0) fetch_offsets(goff, p.global, tr0, has1, p.kt, kt0, min(kOffsetChunk, nk) + 1, lane);
-    if (warp == 1) {
+    if (warp == 0) {
         ptx::tmem_alloc(ptx::smem_addr(tmem_slot), p.tmem_cols);
         ptx::tmem_relinquish();
     }
@@ -132,6 +123,8 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
     ptx::tc_fence_after();
     if (tid == 0) {
         ptx::prefetch_tensormap(&xmap);
+        ptx::prefetch_tensormap(&mmap);
+        for (int i = 0; i < pm.count; ++i) ptx::prefetch_tensormap(&pm.map[i]);
         // Decode lookup tables: one bulk copy from the library's constant table.
         ptx::mbar_arrive_expect_tx(bar_tab, kTableBytes);
         ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
@@ -139,173 +132,190 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer
-        const uint64_t pol_w = ptx::policy_evict_first();
-        const uint64_t pol_x = ptx::policy_evict_last();
-        const int ntiles = has1 ? 2 : 1;
-        bool ok = true;
-        int issued = 0;
-        for (int is = 0; is < nsup; ++is) {
-            const int s = is % p.nstages;
-            const int kb = is * G;             // first local K slice of the slot
-            const int gn = min(G, nk - kb);    // slices in this slot
-            const int ci = kb % kOffsetChunk;  // its index in the offset cache (G divides the chunk)
-            if (kb > 0 && ci == 0) {
-                fetch_offsets(goff, p.global, tr0, has1, p.kt, kt0 + kb,
-                              min(kOffsetChunk, nk - kb) + 1, lane);
-                __syncwarp();
-            }
-            if (is >= p.nstages && lane == 0)
-                ok = ptx::mbar_wait(bar_addr(bar_empty, s), ((is / p.nstages) - 1) & 1);
-            ok = __shfl_sync(kFullMask, ok, 0) != 0;
-            if (!ok) break;
-            const uint32_t slot = sbase + p.off_slots + uint32_t(s) * p.slot.bytes;
-            const uint32_t full = bar_addr(bar_full, s);
-            // Payload runs of the slot's slices. Copies need 16-byte aligned
-            // sources; offsets of valid packed data always are.
-            uint32_t clen[2] = {0, 0}, rlen[2] = {0, 0};
-            int2 g0[2] = {make_int2(0, 0), make_int2(0, 0)};
-            for (int tau = 0; tau < ntiles; ++tau) {
-                const int2* row = goff + tau * (kOffsetChunk + 1) + ci;
-                g0[tau] = row[0];
-                const int dc = row[gn].x - g0[tau].x, dr = row[gn].y - g0[tau].y;
-                if ((g0[tau].x & 15) == 0)
-                    clen[tau] = min(uint32_t(max(dc, 0)), uint32_t(G) * cap_c) & ~15u;
-                if ((g0[tau].y & 7) == 0)
-                    rlen[tau] = (min(uint32_t(max(dr, 0)), uint32_t(G) * cap_r) * 2u) & ~15u;
-            }
-            if (lane == 0) {
-                // Per-slice payload starts within the slot's regions, clamped
-                // so slice g reads inside its region whatever the offsets say.
-                int2* hdr = reinterpret_cast<int2*>(smem + p.off_slots + uint32_t(s) * p.slot.bytes +
-                                                    p.slot.hdr);
-                // A missing second tile row decodes (discarded) zero offsets.
-                uint32_t bytes = p.x_bytes;
-                for (int tau = 0; tau < 2; ++tau) {
-                    const int2* row = goff + tau * (kOffsetChunk + 1) + ci;
-                    for (int g = 0; g < gn; ++g) {
-                        const int dc = row[g].x - g0[tau].x, dr = row[g].y - g0[tau].y;
-                        hdr[tau * kMaxGroup + g] =
-                            tau < ntiles ? make_int2(min(max(dc, 0), int(uint32_t(g) * cap_c)),
-                                                     min(max(dr, 0), int(uint32_t(g) * cap_r)))
-                                         : make_int2(0, 0);
-                    }
-                    if (tau < ntiles)
-                        bytes += 3u * 512u * uint32_t(gn) + 32u * uint32_t(gn) + clen[tau] +
-                                 rlen[tau];
-                }
-                ptx::mbar_arrive_expect_tx(full, bytes);
-            }
-            __syncwarp();
-            // Copies spread over lanes: tile row tau uses lanes 6*tau + {0..5}.
-            if (lane < 6 * ntiles) {
-                const int tau = lane / 6, c = lane % 6;
-                const size_t t = size_t(tr0 + tau) * p.kt + kt0 + kb;
-                if (c < 3) {
-                    const uint64_t* src = c == 0 ? p.b1 : c == 1 ? p.b2 : p.b3;
-                    ptx::bulk_g2s(slot + (tau ? p.slot.plane1 : 0u) + uint32_t(c) * pstride,
-                                  src + t * 64, 512u * uint32_t(gn), full, pol_w);
-                } else if (c == 3) {
-                    ptx::bulk_g2s(slot + p.slot.med + uint32_t(tau) * 32u * G, p.medium + t * 8,
-                                  32u * uint32_t(gn), full, pol_w);
-                } else if (c == 4) {
-                    if (clen[tau])
-                        ptx::bulk_g2s(slot + (tau ? p.slot.common1 : p.slot.common0), p.sm + g0[tau].x,
-                                      clen[tau], full, pol_w);
-                } else if (rlen[tau]) {
-                    ptx::bulk_g2s(slot + (tau ? p.slot.rare1 : p.slot.rare0), p.rare + g0[tau].y,
-                                  rlen[tau], full, pol_w);
-                }
-            } else if (lane == 31) {
-                // x tiles of the slot's K slices: one 3-D box (64 x bn x G);
-                // slices past the end of K arrive zero-filled and are unused.
-                ptx::tma_load_3d(sbase + p.off_x + uint32_t(s) * p.x_bytes, &xmap, 0,
-                                 nblk * p.bn, kt0 + kb, full, pol_x);
-            }
-            ++issued;
-        }
-        // Never leave copies in flight: wait for every issued slot to land.
-        if (lane == 0)
-            for (int is = max(0, issued - p.nstages); is < issued; ++is)
-                ptx::mbar_wait(bar_addr(bar_full, is % p.nstages), (is / p.nstages) & 1);
-        __syncwarp();
-    } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
+        // Slice k = NDG*u + g comes from group g's A buffer 2g + (u & 1)
+        // (use u >> 1) and x slot k % nx. The loop keeps every index as a
+        // counter: this thread shares its sub-partition with decoder warps,
+        // so each instruction here costs several issue cycles.
         if (lane == 0) {
             const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
+            const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
+            const uint32_t abase = tmem + p.a_col0;
+            const int nx = p.nx;
+            int xs = 0;
+            uint32_t xph = 0;
             bool ok = true;
-            for (int is = 0; is < nsup && ok; ++is) {
-                const int s = is % p.nstages, grp = is % NDG, use = is / NDG;
-                const int gn = min(G, nk - is * G);
-                if (!ptx::mbar_wait(bar_addr(bar_full, s), (is / p.nstages) & 1)) break;
-                const uint32_t xslot = sbase + p.off_x + uint32_t(s) * p.x_bytes;
-                for (int gi = 0; gi < gn; ++gi) {
-                    const int a = grp * G + gi;
-                    if (!ptx::mbar_wait(bar_addr(bar_afull, a), use & 1)) {
+            for (int u = 0, k = 0; ok && k < nk; ++u) {
+                const uint32_t aph = uint32_t(u >> 1) & 1u;
+#pragma unroll
+                for (int g = 0; g < NDG; ++g) {
+                    if (k >= nk) break;
+                    const int a = 2 * g + (u & 1);
+                    if (!ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) ||
+                        !ptx::mbar_wait(bar_addr(bar_afull, a), aph)) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
-                    const uint64_t bdesc =
-                        ptx::smem_desc_sw128(xslot + uint32_t(gi * p.bn) * 128u);
+                    const uint64_t bdesc = ptx::smem_desc_sw128(xbase + uint32_t(xs) * xstep);
+                    const uint32_t at = abase + 32u * uint32_t(a);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        ptx::mma_bf16_ts(tmem, tmem + p.a_col0 + 32u * a + 8u * kk, bdesc + 2u * kk,
-                                         idesc, (is | gi | kk) != 0);
+                        ptx::mma_bf16_ts(tmem, at + 8u * kk, bdesc + 2u * kk, idesc, (k | kk) != 0);
                     ptx::mma_commit(bar_addr(bar_aempty, a));
+                    ptx::mma_commit(bar_addr(bar_xempty, xs));
+                    if (++xs == nx) xs = 0, xph ^= 1u;
+                    ++k;
                 }
-                ptx::mma_commit(bar_addr(bar_empty, s));
             }
             ptx::mma_commit(bar_d);  // fires once every issued MMA has finished
         }
         __syncwarp();
+    } else if (warp == 4 * NDG + 1) {
+        // ------------------------------------------------------ x loader
+        // Slice k's x tile goes to x slot k % nx once the MMAs of slice
+        // k - nx have finished reading that slot.
+        if (lane == 0) {
+            const uint64_t pol_x = ptx::policy_evict_last();
+            const int nx = p.nx;
+            int issued = 0;
+            for (int k = 0; k < nk; ++k) {
+                const int xs = k % nx;
+                if (k >= nx && !ptx::mbar_wait(bar_addr(bar_xempty, xs), ((k / nx) - 1) & 1)) break;
+                ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
+                ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0,
+                                 nblk * p.bn, kt0 + k, bar_addr(bar_xfull, xs), pol_x);
+                issued = k + 1;
+            }
+            // Never leave copies in flight: wait for the last loads to land.
+            for (int k = max(0, issued - nx); k < issued; ++k)
+                ptx::mbar_wait(bar_addr(bar_xfull, k % nx), (k / nx) & 1);
+        }
+        __syncwarp();
     } else {
         // ------------------------------------------------------ decoders
-        const int dw = warp - 2, g = dw >> 2, q = warp & 3;
+        const int dw = warp - 1, g = dw >> 2;
+        const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
         const int tau = lane >> 4;
         const bool valid = tau == 0 || has1;
+        const int2* goffs = reinterpret_cast<const int2*>(p.global);
+        const uint64_t pol_w = ptx::policy_evict_first();
         RowDecoder<8 * 128 * NDG> dec;
         dec.init(tables, sbase + p.off_rb + uint32_t(dw * 32 + lane) * 8u, lane, q, p.start_exp);
         const uint32_t trow = tmem + (uint32_t(32 * q) << 16) + p.a_col0;
+
+        // Lanes 0-3 hold the (common, rare) offsets of the group's u-th slice:
+        // lane 2*t + e = entry e (0 start, 1 end) of tile row t.
+        auto load_offsets = [&](int u) {
+            const int k = g + u * NDG;
+            int2 v = make_int2(0, 0);
+            if (k < nk && lane < 4 && ((lane >> 1) == 0 || has1))
+                v = goffs[size_t(tr0 + (lane >> 1)) * p.kt + kt0 + k + (lane & 1)];
+            return v;
+        };
+        // Fill buffer b with the group's u-th slice (its offsets in `o`).
+        auto issue = [&](int u, int b, int2 o) {
+            const int k = g + u * NDG;
+            int2 e[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                e[i].x = __shfl_sync(kFullMask, o.x, i), e[i].y = __shfl_sync(kFullMask, o.y, i);
+            uint32_t clen[2], rlen[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int2 st = e[2 * t], en = e[2 * t + 1];
+                const bool live = t == 0 || has1;
+                // Payload copies need 16-byte aligned sources, which the
+                // offsets of valid packed data always give.
+                clen[t] = live && (st.x & 15) == 0
+                              ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
+                              : 0u;
+                rlen[t] = live && (st.y & 7) == 0
+                              ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
+                              : 0u;
+            }
+            if (lane == 0) {
+                const uint32_t slot = sbase + p.off_slots + uint32_t(g * 2 + b) * L.bytes;
+                const uint32_t full = bar_addr(bar_full, g * 2 + b);
+                const int kc = kt0 + k;
+                if (q == 1) {
+                    ptx::mbar_arrive_expect_tx(full, p.plane_box_bytes + 64u + clen[0] + clen[1] +
+                                                         rlen[0] + rlen[1]);
+                    if (pm.count == 1) {
+                        ptx::tma_load_4d(slot, &pm.map[0], 0, kc, tr0, 0, full, pol_w);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 3; ++i)
+                            ptx::tma_load_3d(slot + uint32_t(i) * L.plane_stride, &pm.map[i], 0, kc,
+                                             tr0, full, pol_w);
+                    }
+                } else if (q == 2) {
+                    ptx::tma_load_3d(slot + L.med, &mmap, 0, kc, tr0, full, pol_w);
+                    if (clen[0]) ptx::bulk_g2s(slot + L.common0, p.sm + e[0].x, clen[0], full, pol_w);
+                } else if (q == 3) {
+                    if (clen[1]) ptx::bulk_g2s(slot + L.common1, p.sm + e[2].x, clen[1], full, pol_w);
+                } else {
+                    if (rlen[0]) ptx::bulk_g2s(slot + L.rare0, p.rare + e[0].y, rlen[0], full, pol_w);
+                    if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[2].y, rlen[1], full, pol_w);
+                }
+            }
+        };
+
+        const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
+        {
+            const int2 o0 = load_offsets(0), o1 = load_offsets(1);
+            if (nu > 0) issue(0, 0, o0);
+            if (nu > 1) issue(1, 1, o1);
+        }
+        int2 onext = load_offsets(2);
         uint32_t out[32];
         bool ok = ptx::mbar_wait(bar_tab, 0);
-        for (int is = g; is < nsup; is += NDG) {
-            const int s = is % p.nstages, use = is / NDG;
-            const int gn = min(G, nk - is * G);
-            ok = ok && ptx::mbar_wait(bar_addr(bar_full, s), (is / p.nstages) & 1);
-            if (!__all_sync(kFullMask, ok)) break;
-            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(s) * p.slot.bytes);
-            const uint32_t plane = slot + (tau ? p.slot.plane1 : 0u);
-            const uint32_t med = slot + p.slot.med + uint32_t(tau) * 32u * G;
-            const uint32_t com = slot + (tau ? p.slot.common1 : p.slot.common0);
-            const uint32_t rar = slot + (tau ? p.slot.rare1 : p.slot.rare0);
-            for (int gi = 0; gi < gn; ++gi) {
-                const int a = g * G + gi;
-                if (use > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (use - 1) & 1);
-                if (!__all_sync(kFullMask, ok)) break;
-                const int2 hdr = ptx::lds_s64(slot + p.slot.hdr + uint32_t(tau * kMaxGroup + gi) * 8u);
-                dec.decode(plane + 512u * uint32_t(gi), pstride, med + 32u * uint32_t(gi),
-                           com + uint32_t(hdr.x), rar + 2u * uint32_t(hdr.y), cap_c, cap_r, out);
+        int waited = 0;  // uses whose slot this warp saw land
+        for (int u = 0; u < nu; ++u) {
+            const int b = u & 1;
+            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(g * 2 + b) * L.bytes);
+            ok = ok && ptx::mbar_wait(bar_addr(bar_full, g * 2 + b), (u >> 1) & 1);
+            ok = __all_sync(kFullMask, ok);
+            if (ok) {
+                waited = u + 1;
+                dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
+                           slot + L.med + uint32_t(tau) * 32u,
+                           slot + (tau ? L.common1 : L.common0),
+                           slot + (tau ? L.rare1 : L.rare0), cap_c, cap_r, out);
                 if (!valid) {
 #pragma unroll
                     for (int w = 0; w < 32; ++w) out[w] = 0;
                 }
-                __syncwarp();
-                ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
-                ptx::tmem_wait_st();
-                ptx::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(bar_addr(bar_afull, a));
+                // The A buffer is free once the MMAs of its previous use finished.
+                const int a = 2 * g + (u & 1), ause = u >> 1;
+                if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
+                ok = __all_sync(kFullMask, ok);
+                if (ok) {
+                    ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
+                    ptx::tmem_wait_st();
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(bar_addr(bar_afull, a));
+                }
             }
-            if (!__all_sync(kFullMask, ok)) break;
-            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_empty, s));
+            // Every warp of the group passes here once per slice, failed or
+            // not: after it the group's reads of buffer b are over.
+            named_sync(1 + g, 128);
+            if (ok && u + 2 < nu) issue(u + 2, b, onext);
+            onext = load_offsets(u + 3);
         }
+        // Never leave copies in flight: after a failure, wait (bounded) for
+        // the slots this warp issued into but did not see land.
+        if (!ok && lane == 0)
+            for (int u = waited; u < min(nu, waited + 2); ++u)
+                ptx::mbar_wait(bar_addr(bar_full, g * 2 + (u & 1)), (u >> 1) & 1);
+        __syncwarp();
     }
 
     // ---------------------------------------------------------- epilogue
     float* red = reinterpret_cast<float*>(smem + p.off_x);  // [bn][128] FP32 when S > 1
-    if (warp >= 2) {
-        const int dw = warp - 2, g = dw >> 2, q = warp & 3;
+    if (warp >= 1 && warp <= 4 * NDG) {
+        const int dw = warp - 1, g = dw >> 2, q = warp & 3;
         const bool dok = ptx::mbar_wait(bar_d, 0);
         ptx::tc_fence_after();
         const int row = 32 * q + lane;  // TMEM lane = slot in the reduction tile
@@ -359,7 +369,7 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
         ptx::cluster_sync();  // partners may still read this CTA's tile until here
     }
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 0) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, p.tmem_cols);
     }
@@ -415,27 +425,27 @@ DeviceInfo& device_info(int device) {
 uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct GemmLayout {
-    uint32_t off_rb, off_goff, off_x, off_slots, x_bytes, total;
+    uint32_t off_rb, off_x, off_slots, x_bytes, total;
     SlotLayout slot;
-    int nstages;
+    int nx;
 };
 
-// Shared memory: barriers | lookup tables | row buffers | offset cache |
-// x ring (1024-aligned, group*bn*128 bytes per slot) | compressed ring | pad.
-GemmLayout gemm_layout(int ndg, int group, int bn, uint32_t cap_c, uint32_t cap_r,
+// Shared memory: barriers | lookup tables | row buffers | x ring (1024-
+// aligned, nx slots of bn*128 bytes) | compressed slots (two per decoder
+// group) | pad. The x ring takes what the rest leaves, up to kMaxX slots.
+GemmLayout gemm_layout(int ndg, int bn, uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r,
                        int smem_limit) {
     GemmLayout l{};
     l.off_rb = kBarrierBytes + kTableBytes;
-    l.off_goff = l.off_rb + uint32_t(128 * ndg) * kRowBufferBytes;
-    l.off_x = round_up(l.off_goff + 2 * (kOffsetChunk + 1) * 8, 1024);
-    l.x_bytes = uint32_t(group * bn) * 128;
-    l.slot = slot_layout(group, cap_c, cap_r);
-    const uint32_t per_stage = l.x_bytes + l.slot.bytes;
-    const uint32_t used = l.off_x + kRingPadBytes;
+    l.off_x = round_up(l.off_rb + uint32_t(128 * ndg) * kRowBufferBytes, 1024);
+    l.x_bytes = uint32_t(bn) * 128;
+    l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r);
+    const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
+    const uint32_t used = l.off_x + slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    l.nstages = std::min<int>(kMaxStages, int(avail / per_stage)) / ndg * ndg;
-    l.off_slots = l.off_x + uint32_t(l.nstages) * l.x_bytes;
-    l.total = l.off_slots + uint32_t(l.nstages) * l.slot.bytes + kRingPadBytes;
+    l.nx = std::min<int>(kMaxX, int(avail / l.x_bytes));
+    l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
+    l.total = l.off_slots + slots + kRingPadBytes;
     return l;
 }
 
@@ -443,29 +453,47 @@ GemmLayout gemm_layout(int ndg, int group, int bn, uint32_t cap_c, uint32_t cap_
 
 int device_sm_count(int device) { return device_info(device).sms; }
 
-SlotLayout slot_layout(int group, uint32_t cap_c, uint32_t cap_r) {
+SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r) {
+    // One K slice of two tile rows. A bitmap plane's tile occupies
+    // plane_pitch bytes (576: the tensor load's box is 72 words wide, the 8
+    // words past the 64-word tile zero-filled, which puts tile row 1 64
+    // bytes off modulo 128).
     SlotLayout s{};
-    const uint32_t g = uint32_t(group);
-    const uint32_t planes = 3u * 512u * g;
-    s.plane1 = planes + 64;
-    s.med = s.plane1 + planes;
-    s.hdr = s.med + 2u * 32u * g;
-    s.common0 = round_up(s.hdr + 2u * kMaxGroup * 8u, 128);
-    s.common1 = s.common0 + g * cap_c + 64;  // cap_c is a multiple of 128
-    s.rare0 = round_up(s.common1 + g * cap_c, 16);
-    s.rare1 = s.rare0 + g * cap_r * 2;
-    s.bytes = round_up(s.rare1 + g * cap_r * 2, 128);
+    s.plane1 = plane_pitch;
+    s.plane_stride = 2u * plane_pitch;
+    s.med = round_up(3u * s.plane_stride, 128);  // [2][32 B]
+    s.hdr = 0;                                   // unused: one slice per slot
+    s.common0 = round_up(s.med + 64u, 128);
+    s.common1 = s.common0 + cap_c + 64;  // cap_c is a multiple of 128
+    s.rare0 = round_up(s.common1 + cap_c, 16);
+    s.rare1 = s.rare0 + cap_r * 2;
+    s.bytes = round_up(s.rare1 + cap_r * 2, 128);
     return s;
 }
 
-static bool encode_map(CUtensorMap* map, const void* base, cuuint32_t rank,
-                       const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box) {
+SlotLayout decompress_slot_layout(int half, uint32_t cap_c, uint32_t cap_r) {
+    SlotLayout s{};
+    const uint32_t h = uint32_t(half);
+    s.plane1 = 512u * h;           // second half of each plane
+    s.plane_stride = 2u * 512u * h;
+    s.med = 3u * s.plane_stride;   // [2*half][32 B]
+    s.hdr = s.med + 2u * h * 32u;
+    s.common0 = round_up(s.hdr + 2u * kMaxGroup * 8u, 128);
+    s.common1 = s.common0 + h * cap_c + 64;
+    s.rare0 = round_up(s.common1 + h * cap_c, 16);  // one run for the whole chunk
+    s.rare1 = s.rare0;
+    s.bytes = round_up(s.rare0 + 2u * h * cap_r * 2, 128);
+    return s;
+}
+
+static bool encode_map(CUtensorMap* map, CUtensorMapDataType type, const void* base,
+                       cuuint32_t rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                       const cuuint32_t* box, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
-    const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
-              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return fn(map, type, rank, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -474,7 +502,33 @@ bool encode_tensor_map_2d(CUtensorMap* map, const void* base, uint64_t inner, ui
     const cuuint64_t dims[2] = {inner, outer};
     const cuuint64_t strides[1] = {row_bytes};
     const cuuint32_t box[2] = {box_inner, box_outer};
-    return encode_map(map, base, 2, dims, strides, box);
+    return encode_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, 2, dims, strides, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool encode_plane_maps(PlaneMaps* maps, const void* b1, const void* b2, const void* b3,
+                       uint64_t inner, uint64_t outer, uint32_t box_words, uint32_t box_inner,
+                       uint32_t box_outer) {
+    // A plane: [outer][inner] tiles of 64 u64 words (512 B); the box is
+    // box_words wide (> 64: zero-filled padding after each tile).
+    const cuuint64_t dims[4] = {64, inner, outer, 3};
+    const cuuint32_t box[4] = {box_words, box_inner, box_outer, 3};
+    const auto a1 = reinterpret_cast<uintptr_t>(b1), a2 = reinterpret_cast<uintptr_t>(b2),
+               a3 = reinterpret_cast<uintptr_t>(b3);
+    if (a2 > a1 && a2 - a1 == a3 - a2 && (a2 - a1) % 16 == 0 && a2 - a1 < (uint64_t(1) << 40)) {
+        const cuuint64_t strides[3] = {512, inner * 512, a2 - a1};
+        maps->count = 1;
+        return encode_map(&maps->map[0], CU_TENSOR_MAP_DATA_TYPE_UINT64, b1, 4, dims, strides,
+                          box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    const cuuint64_t strides[2] = {512, inner * 512};
+    const void* planes[3] = {b1, b2, b3};
+    maps->count = 3;
+    for (int i = 0; i < 3; ++i)
+        if (!encode_map(&maps->map[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, planes[i], 3, dims,
+                        strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    return true;
 }
 
 static int tile_n(int n) { return n > 256 ? 256 : std::max(16, (n + 15) / 16 * 16); }
@@ -565,10 +619,6 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     GemmParams p{};
     p.sm = static_cast<const uint8_t*>(sm);
     p.rare = static_cast<const uint16_t*>(rare);
-    p.b1 = static_cast<const uint64_t*>(b1);
-    p.b2 = static_cast<const uint64_t*>(b2);
-    p.b3 = static_cast<const uint64_t*>(b3);
-    p.medium = static_cast<const int*>(medium);
     p.global = static_cast<const int*>(global);
     p.y = static_cast<uint16_t*>(y);
     p.m = m, p.n = n, p.k = k, p.kt = kt, p.row_tiles = m / 64;
@@ -577,44 +627,66 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.cap_c = common_capacity(max_common);
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
-    // (decoder groups, K slices per slot), most parallel first. Four groups
-    // need a ring of at least four slots, two groups of two.
-    struct Choice {
-        int ndg, group;
-    };
-    constexpr Choice kChoices[] = {{4, 2}, {2, 4}, {2, 2}, {2, 1}};
+    // Bitmap tensor maps: 72-word boxes (bank offset for tile row 1) when the
+    // driver accepts a box wider than the tile, else 64.
+    PlaneMaps pm;
+    uint32_t pitch = 576;
+    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 72, 1, 2)) {
+        pitch = 512;
+        if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 64, 1, 2)) {
+            zs_set_error("zipgemm: bitmap tensor maps rejected (bitmaps must be 16-byte aligned)");
+            return cudaErrorInvalidValue;
+        }
+    }
+    p.plane_box_bytes = 3u * 2u * pitch;
+    // Band offsets as [row tiles][k tiles][4 u64]: one box = both tile rows.
+    CUtensorMap mmap;
+    {
+        const cuuint64_t dims[3] = {4, uint64_t(kt), uint64_t(m / 64)};
+        const cuuint64_t strides[2] = {32, uint64_t(kt) * 32};
+        const cuuint32_t box[3] = {4, 1, 2};
+        if (!encode_map(&mmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, medium, 3, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE)) {
+            zs_set_error("zipgemm: band-offset tensor map rejected (must be 16-byte aligned)");
+            return cudaErrorInvalidValue;
+        }
+    }
+    // Four decoder groups when the x ring still gets three slots (the MMA
+    // runs two slices ahead of the x loads), else two.
     int ndg = 0;
     GemmLayout l{};
-    for (const Choice& c : kChoices) {
-        l = gemm_layout(c.ndg, c.group, p.bn, p.cap_c, p.cap_r, d.smem_optin);
-        if (l.nstages >= c.ndg && c.ndg * c.group <= kMaxABuffers) {
-            ndg = c.ndg;
-            p.group = c.group;
+    for (int cand : {4, 2}) {
+        l = gemm_layout(cand, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
+        if (l.nx >= 3 || (cand == 2 && l.nx >= 2)) {
+            ndg = cand;
             break;
         }
     }
     if (!ndg) {
-        zs_set_error("zipgemm: packed payload capacity leaves no room for a two-slot ring");
+        zs_set_error("zipgemm: packed payload capacity leaves no room for the shared-memory rings");
         return cudaErrorInvalidConfiguration;
     }
     // Split-K reduction reuses the rings: they must hold a bn x 128 FP32 tile.
     if (kparts > 1 && uint32_t(p.bn) * 128 * 4 > l.total - kRingPadBytes - l.off_x)
         kparts = p.kparts = 1;
-    p.nstages = l.nstages;
-    p.off_rb = l.off_rb, p.off_goff = l.off_goff, p.off_x = l.off_x;
+    p.nx = l.nx;
+    p.off_rb = l.off_rb, p.off_x = l.off_x;
     p.off_slots = l.off_slots, p.x_bytes = l.x_bytes, p.slot = l.slot;
     p.a_col0 = uint32_t(std::max(p.bn, 32));
+    // Two A buffers per group when they fit in the A-buffer barriers and TMEM.
+    // Two TMEM A buffers per decoder group (a_col0 + 64 * ndg <= 512 columns).
     uint32_t cols = 32;
-    while (cols < p.a_col0 + 32u * uint32_t(ndg * p.group)) cols <<= 1;
+    while (cols < p.a_col0 + 64u * uint32_t(ndg)) cols <<= 1;
     p.tmem_cols = cols;
 
-    // x viewed as [K/64][N][64]: one box = `group` consecutive K slices of
-    // bn tokens, each slice a 128-byte-swizzled bn x 64 tile.
+    // x viewed as [K/64][N][64]: one box = one K slice of bn tokens, a
+    // 128-byte-swizzled bn x 64 tile.
     CUtensorMap xmap;
     const cuuint64_t dims[3] = {64, uint64_t(n), uint64_t(kt)};
     const cuuint64_t strides[2] = {uint64_t(k) * 2, 128};
-    const cuuint32_t box[3] = {64, uint32_t(p.bn), uint32_t(p.group)};
-    if (!encode_map(&xmap, x, 3, dims, strides, box)) {
+    const cuuint32_t box[3] = {64, uint32_t(p.bn), 1};
+    if (!encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, 3, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B)) {
         zs_set_error("zipgemm: activation tensor map rejected (x must be 16-byte aligned)");
         return cudaErrorInvalidValue;
     }
@@ -631,14 +703,14 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = ndg == 4 ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<4>, xmap, p)
-                 : cudaLaunchKernelEx(&cfg, zipgemm_kernel<2>, xmap, p);
+    e = ndg == 4 ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<4>, xmap, pm, mmap, p)
+                 : cudaLaunchKernelEx(&cfg, zipgemm_kernel<2>, xmap, pm, mmap, p);
     if (e != cudaSuccess) {
         char msg[220];
         snprintf(msg, sizeof(msg),
-                 "zipgemm launch (grid %u x %u, cluster %d, %u B shared, %d slots x %d slices, "
-                 "bn %d): %s",
-                 cfg.gridDim.x, cfg.gridDim.y, kparts, l.total, l.nstages, p.group, p.bn,
+                 "zipgemm launch (grid %u x %u, cluster %d, %u B shared, %d decoder groups, "
+                 "%d x slots, bn %d): %s",
+                 cfg.gridDim.x, cfg.gridDim.y, kparts, l.total, ndg, l.nx, p.bn,
                  cudaGetErrorString(e));
         zs_set_error(msg);
     }

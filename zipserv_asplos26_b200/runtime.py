@@ -139,10 +139,29 @@ class PackedWeight:
         return sum(buffer.numel() for buffer in self.buffers)
 
     def to(self, device: torch.device | str) -> "PackedWeight":
-        """Transfer packed bytes without changing their representation."""
+        """Transfer packed bytes without changing their representation.
+
+        On a GPU the seven streams share one allocation, each at a 256-byte
+        aligned offset: the three equally sized bitmap planes then sit at equal
+        distances, which lets the kernels fetch all three with one tensor copy.
+        """
+        device = torch.device(device)
+        if device.type != "cuda":
+            buffers = tuple(buffer.to(device) for buffer in self.buffers)
+        else:
+            offsets, total = [], 0
+            for buffer in self.buffers:
+                offsets.append(total)
+                total += (buffer.numel() + 255) // 256 * 256
+            storage = torch.empty(max(total, 256), dtype=torch.uint8, device=device)
+            views = []
+            for buffer, offset in zip(self.buffers, offsets, strict=True):
+                view = storage[offset:offset + buffer.numel()]
+                view.copy_(buffer)
+                views.append(view)
+            buffers = tuple(views)
         return PackedWeight(
-            tuple(buffer.to(device) for buffer in self.buffers),
-            self.m, self.k, self.max_common, self.max_rare, self.start_exp,
+            buffers, self.m, self.k, self.max_common, self.max_rare, self.start_exp,
         )
 
 
