@@ -1,0 +1,211 @@
+"""The product's host packer against the reference (CPU only).
+
+* ``zipserv_compress`` (include/zipserv_bridge.h; reference
+  integrations/vllm/native/host_bridge.cpp:18-43) must reproduce the
+  reference bridge byte for byte on the seeded Llama-like weights.
+* ``InitBF16MatrixTripleBitmap`` (include/L_API.h; reference
+  csrc/L_API.cu:411-455) with an explicit 7-exponent window must reproduce
+  all eight buffers of every reference encoder case
+  (tests/test_host_packer.cpp:69-111), for 1, 2 and 4 packing workers.
+* Invalid inputs fail without leaking or half-filling the descriptor
+  (tests/test_host_packer.cpp:122-141, host_bridge.cpp:19-20); concurrent
+  calls are independent (tests/test_host_packer.cpp:113-121).
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import json
+import subprocess
+import threading
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from zipserv_asplos26_b200 import runtime
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _sha_bytes(ptr: int, n: int) -> str:
+    return hashlib.sha256(ctypes.string_at(ptr, n) if n else b"").hexdigest()
+
+
+def compress(lib, words: np.ndarray):
+    words = np.ascontiguousarray(words, dtype=np.uint16)
+    m, k = words.shape
+    out = runtime._NativePacked()
+    status = lib.zipserv_compress(words.ctypes.data, m, k, ctypes.byref(out))
+    return status, out
+
+
+def _init_symbol(native_lib) -> str:
+    path = runtime.library_path()
+    names = subprocess.run(["nm", "-D", "--defined-only", str(path)], check=True,
+                           capture_output=True, text=True).stdout.split()
+    matches = [n for n in names if "InitBF16MatrixTripleBitmap" in n]
+    assert len(matches) == 1, matches
+    return matches[0]
+
+
+@pytest.fixture(scope="module")
+def init_api(native_lib):
+    fn = getattr(native_lib, _init_symbol(native_lib))
+    pp = ctypes.POINTER(ctypes.c_void_p)
+    fn.argtypes = ([ctypes.c_void_p] + [ctypes.c_int] * 8 + [ctypes.POINTER(ctypes.c_int)] +
+                   [pp] * 8 + [ctypes.POINTER(ctypes.c_int)] * 2)
+    fn.restype = ctypes.c_int
+    return fn
+
+
+_libc = ctypes.CDLL(None)
+_libc.free.argtypes = [ctypes.c_void_p]
+
+
+def init_pack(init_api, words: np.ndarray, base: int):
+    """Returns (tiles, max_common, max_rare, [8 sha256]) or the error code."""
+    words = np.ascontiguousarray(words, dtype=np.uint16)
+    m, k = words.shape
+    exps = (ctypes.c_int * 7)(*[base + i for i in range(7)])
+    ptrs = [ctypes.c_void_p() for _ in range(8)]
+    mc, mr = ctypes.c_int(-7), ctypes.c_int(-7)
+    tiles = init_api(words.ctypes.data, m, k, 8, 16, 64, 8, 64, 64, exps,
+                     *[ctypes.byref(p) for p in ptrs], ctypes.byref(mc), ctypes.byref(mr))
+    if tiles < 0:
+        assert all(not p.value for p in ptrs)
+        return tiles
+    try:
+        glob = np.ctypeslib.as_array(ctypes.cast(ptrs[7], ctypes.POINTER(ctypes.c_int32)),
+                                     shape=(2 * (tiles + 1),))
+        lengths = [int(glob[2 * tiles]), int(glob[2 * tiles + 1]) * 2, 512 * tiles,
+                   512 * tiles, 512 * tiles, 512 * tiles, 32 * tiles, 8 * (tiles + 1)]
+        digests = [_sha_bytes(p.value, n) for p, n in zip(ptrs, lengths)]
+    finally:
+        for p in ptrs:
+            _libc.free(p)
+    return tiles, mc.value, mr.value, digests
+
+
+def test_compress_matches_reference_bridge(native_lib, oracle_mod):
+    golden = json.loads((GOLDEN / "reference_bridge.json").read_text())
+    for label, want in golden.items():
+        w = oracle_mod.llama_weight(want["m"], want["k"], want["seed"], want["outliers"])
+        status, out = compress(native_lib, w)
+        assert status == 0, native_lib.zipserv_error()
+        try:
+            assert list(out.lengths) == want["lengths"], label
+            assert [_sha_bytes(out.buffers[i], out.lengths[i]) for i in range(7)] == want["sha256"]
+            assert (out.m, out.k, out.max_common, out.max_rare, out.start_exp) == (
+                want["m"], want["k"], want["max_common"], want["max_rare"], want["start_exp"])
+        finally:
+            native_lib.zipserv_free(ctypes.byref(out))
+        assert not any(out.buffers)  # host_bridge.cpp:14-16 nulls the pointers
+
+
+@pytest.mark.parametrize("workers", ["1", "2", "4"])
+def test_legacy_init_api_matches_every_reference_case(init_api, oracle_mod, monkeypatch, workers):
+    monkeypatch.setenv("ZIPSERV_PACK_WORKERS", workers)
+    golden = json.loads((GOLDEN / "reference_packer.json").read_text())
+    for name, words, m, k, _base, small in oracle_mod.host_packer_cases():
+        want = golden[name]
+        result = init_pack(init_api, words, want["base"])
+        assert not isinstance(result, int), (name, result)
+        tiles, mc, mr, digests = result
+        assert (tiles, mc, mr) == (want["tiles"], want["max_common"], want["max_rare"]), name
+        for i in range(8):
+            if i == 5 and not small:
+                continue  # the reference case ran without small offsets
+            assert digests[i] == want["sha256"][i], (name, i)
+
+
+def test_init_api_rejects_bad_windows_and_tiles(init_api):
+    words = np.zeros((64, 64), dtype=np.uint16)
+    m, k = words.shape
+
+    def call(exps, tiles=(8, 16, 64, 8, 64, 64), mat=(m, k)):
+        arr = (ctypes.c_int * 7)(*exps)
+        ptrs = [ctypes.c_void_p() for _ in range(8)]
+        mc, mr = ctypes.c_int(0), ctypes.c_int(0)
+        r = init_api(words.ctypes.data, *mat, *tiles, arr, *[ctypes.byref(p) for p in ptrs],
+                     ctypes.byref(mc), ctypes.byref(mr))
+        if r >= 0:
+            for p in ptrs:
+                _libc.free(p)
+        else:
+            assert all(not p.value for p in ptrs)
+        return r
+
+    assert call(range(100, 107)) == 1
+    assert call([100, 101, 102, 104, 105, 106, 107]) == -1      # not consecutive
+    assert call(range(250, 257)) == -1                          # past 255
+    assert call(range(-1, 6)) == -1
+    assert call(range(100, 107), tiles=(8, 16, 64, 8, 64, 32)) == -1
+    assert call(range(100, 107), mat=(65, 64)) == -1
+    assert call(range(100, 107), mat=(64, 0)) == -1
+
+
+def test_invalid_compress_inputs_leave_an_empty_descriptor(native_lib):
+    w = np.zeros((64, 64), dtype=np.uint16)
+    for m, k in ((0, 64), (64, 0), (-64, 64), (65, 64), (64, 96), (1 << 16, 1 << 16)):
+        out = runtime._NativePacked()
+        out.m = 99
+        assert native_lib.zipserv_compress(w.ctypes.data, m, k, ctypes.byref(out)) == -1
+        assert native_lib.zipserv_error()
+        assert not any(out.buffers) and not any(out.lengths) and out.m == 0
+    out = runtime._NativePacked()
+    assert native_lib.zipserv_compress(None, 64, 64, ctypes.byref(out)) == -1
+    assert native_lib.zipserv_compress(w.ctypes.data, 64, 64, None) == -1
+    native_lib.zipserv_free(None)  # tolerated
+
+
+def test_round_trip_special_values(native_lib, oracle_mod):
+    """All-bits, zeros, -0, NaN, Inf and transposed inputs decode bit for bit
+    (tests/test_host_runtime.py:128-147)."""
+    rng = np.random.default_rng(4)
+    normal = (rng.standard_normal((128, 192)) * 0.02).astype(np.float32)
+    normal_bits = oracle_mod.f32_to_bf16(normal)
+    cases = {
+        "all_bits": np.arange(65536, dtype=np.uint32).astype(np.uint16).reshape(256, 256),
+        "zeros": np.zeros((64, 128), dtype=np.uint16),
+        "neg_zero": np.full((64, 64), 0x8000, dtype=np.uint16),
+        "nan": np.full((64, 64), 0x7FC0, dtype=np.uint16),
+        "inf": np.full((128, 64), 0x7F80, dtype=np.uint16),
+        "normal": normal_bits,
+        "transposed": np.ascontiguousarray(normal_bits.T),
+    }
+    for name, words in cases.items():
+        status, out = compress(native_lib, words)
+        assert status == 0, name
+        try:
+            bufs = [np.ctypeslib.as_array(ctypes.cast(out.buffers[i], ctypes.POINTER(ctypes.c_uint8)),
+                                          shape=(out.lengths[i],)).copy() if out.lengths[i]
+                    else np.zeros(0, np.uint8) for i in range(7)]
+            restored = oracle_mod.decode(bufs, out.m, out.k, out.start_exp)
+            assert np.array_equal(restored, words), name
+        finally:
+            native_lib.zipserv_free(ctypes.byref(out))
+
+
+def test_concurrent_compress_calls_are_independent(native_lib, oracle_mod):
+    weights = [oracle_mod.llama_weight(256, 512, seed=s) for s in range(4)]
+    expected = []
+    for w in weights:
+        status, out = compress(native_lib, w)
+        assert status == 0
+        expected.append([_sha_bytes(out.buffers[i], out.lengths[i]) for i in range(7)])
+        native_lib.zipserv_free(ctypes.byref(out))
+    results = [None] * 4
+
+    def work(i):
+        status, out = compress(native_lib, weights[i])
+        results[i] = (status, [_sha_bytes(out.buffers[j], out.lengths[j]) for j in range(7)])
+        native_lib.zipserv_free(ctypes.byref(out))
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for i in range(4):
+        assert results[i] == (0, expected[i])

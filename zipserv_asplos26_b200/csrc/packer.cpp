@@ -68,6 +68,11 @@ void for_ranges(int count, unsigned workers, const Fn& fn) {
 }  // namespace
 
 unsigned default_workers(int tiles) {
+    // ZIPSERV_PACK_WORKERS (1..64) pins the count; the output never depends on it.
+    if (const char* env = std::getenv("ZIPSERV_PACK_WORKERS")) {
+        const long v = std::strtol(env, nullptr, 10);
+        if (v >= 1 && v <= 64) return unsigned(v);
+    }
     const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
     // About 256 tiles (1M words) per worker keeps thread start-up negligible.
     return std::max(1u, std::min({hw, 64u, unsigned(tiles / 256)}));

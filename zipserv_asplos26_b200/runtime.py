@@ -278,6 +278,8 @@ def linear_kparts(x: Tensor, packed: PackedWeight, k_parts: int,
     m, k = packed.m, packed.k
     if x.dtype != torch.bfloat16 or x.shape[-1] != k:
         raise ValueError("ZipServ linear requires BF16 activations with the matching input width")
+    if x.device.type != "cuda":
+        raise ValueError("ZipServ linear runs on CUDA tensors only")
     _validate_buffers(list(packed.buffers), x.device)
     n = x.numel() // k
     flat = x.reshape(n, k).contiguous()
