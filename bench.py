@@ -72,14 +72,18 @@ class ClockSampler:
 
     def __enter__(self):
         cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-               "-lms", "200"]
+               "-lms", "50"]
         if self.device_id:
             cmd += ["-i", self.device_id]
+        self.started = threading.Event()
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                          text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # The timed region starts only once nvidia-smi is producing samples.
+            self.started.wait(timeout=10)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
@@ -87,6 +91,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.started.set()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -280,6 +285,7 @@ def run_ours(args, world: int, rank: int) -> dict | None:
                           "speedup_vs_cublas": round(dus / us, 3)})
     traffic = _traffic_record()
     launches = len(calls) * steps
+    avg_launch_bytes = step_bytes / len(calls)
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -308,7 +314,9 @@ def run_ours(args, world: int, rank: int) -> dict | None:
             "unit": "GB/s",
             "frac": round(value / peaks["hbm_gbs"], 4),
             "peak_source": peaks["source"],
-            "traffic": traffic.get("traffic_bytes_per_launch"),
+            "traffic": (round(traffic["ratio"] * avg_launch_bytes)
+                        if traffic.get("ratio") else None),
+            "algorithmic_bytes_per_launch": round(avg_launch_bytes),
             "traffic_note": traffic.get("note"),
         },
         "cublas_bf16": {
@@ -341,10 +349,22 @@ class _Null:
 
 
 def _traffic_record() -> dict:
-    path = ROOT / "profiles" / "zipgemm_traffic.json"
+    """DRAM bytes / algorithmic bytes of one ncu-captured ZipGEMM launch
+    (profiles/zipgemm_o16_traffic.txt, ``key: value`` lines)."""
+    path = ROOT / "profiles" / "zipgemm_o16_traffic.txt"
+    rec = {}
     if path.is_file():
-        return json.loads(path.read_text())
-    return {"traffic_bytes_per_launch": None, "note": "no ncu capture recorded"}
+        for line in path.read_text().splitlines():
+            key, sep, value = line.partition(":")
+            if sep:
+                rec[key.strip()] = value.strip()
+    try:
+        ratio = float(rec["dram_bytes_per_launch"]) / float(rec["algorithmic_bytes_per_launch"])
+    except (KeyError, ValueError, ZeroDivisionError):
+        return {"ratio": None, "note": "no ncu capture recorded"}
+    return {"ratio": ratio,
+            "note": f"dram__bytes_read+write / algorithmic bytes = {ratio:.4f} on "
+                    f"{rec.get('launch', 'one launch')}; scaled to the average launch"}
 
 
 def _cpu_case(name: str, n: int, threads: int):
@@ -446,7 +466,7 @@ def run_profile_case(spec: str, repeats: int) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--tokens", type=int, nargs="*", default=list(TOKENS))
