@@ -8,20 +8,20 @@
 //   warp 0      allocates tensor memory; lane 0 issues tcgen05.mma
 //               (A = decoded W slice read from TMEM, B = x tile from shared
 //               memory, 128-byte swizzle, D = FP32 accumulator in TMEM);
-//   last warp   keeps an x ring of nx slices filled with 3-D TMA loads;
 //   warps 1..   NDG decoder groups of four warps. Group g decodes K slices
 //               g, g+NDG, ... from two compressed slots it owns: while it
-//               decodes one, the other is filling. The group issues its own
-//               copies (one 4-D tensor load for the three bitmap planes of
-//               both tile rows, one 3-D load for the band offsets, one bulk
-//               copy per payload run), lane 0 of each of its warps taking a
-//               share: an SM's copy engine takes ~100 cycles per copy, so
-//               copies are few, large and issued from four sub-partitions.
-//               Warp w decodes 16-row band w%4 of both tiles (row = tile*64 +
-//               16*band + i, TMEM lane = 32*band + 16*tile + i); each thread
-//               rebuilds one W row (64 BF16) per slice and stores it with
-//               tcgen05.st into one of the group's TMEM A buffers, so decoded
-//               weights never touch shared memory.
+//               decodes one, the other is filling. Warp w decodes 16-row
+//               band w%4 of both tiles (row = tile*64 + 16*band + i, TMEM
+//               lane = 32*band + 16*tile + i); each thread rebuilds one W row
+//               (64 BF16) per slice and stores it with tcgen05.st into one of
+//               the group's two TMEM A buffers, so decoded weights never
+//               touch shared memory;
+//   next warp   keeps an x ring of nx slices filled with 3-D TMA loads;
+//   last two    producers: fill the groups' slots as soon as a group releases
+//               one, with few, large copies (an SM's copy engine takes ~100
+//               cycles per copy whatever its size): one 4-D tensor load for
+//               the three bitmap planes of both tile rows, one 3-D load for
+//               the band offsets, one bulk copy per payload run.
 // Split-K: the CTAs of a thread-block cluster (1..16) share one row block and
 // split its K slices. Each writes its FP32 accumulator tile to its own shared
 // memory; after a cluster barrier every CTA reduces a disjoint part of the
@@ -49,8 +49,8 @@
 
 namespace zs {
 
-constexpr int kGemmThreads4 = 64 + 128 * 4;
-constexpr int kGemmThreads2 = 64 + 128 * 2;
+constexpr int kGemmThreads4 = 128 + 128 * 4;
+constexpr int kGemmThreads2 = 128 + 128 * 2;
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
 __host__ __device__ __forceinline__ int lane_row(int slot) {
@@ -62,26 +62,24 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
     return base + 8u * uint32_t(index);
 }
 
-__device__ __forceinline__ void named_sync(int id, int threads) {
-    asm volatile("barrier.cta.sync.aligned %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 // Warp roles: warp 0 allocates TMEM and its lane 0 issues the MMAs; warps
-// 1 .. 4*NDG form NDG decoder groups; the last warp keeps the x ring filled. Group g decodes K slices
+// 1 .. 4*NDG form NDG decoder groups; warp 4*NDG+1 keeps the x ring filled;
+// the last two warps fill the decoder groups' compressed slots. Group g decodes K slices
 // g, g + NDG, ... and owns two compressed slots: while it decodes slice u
 // from one, the other is being filled with its next slice. A group issues
 // its own copies after a group barrier (no dedicated producer warp), lane 0
 // of each of its four warps taking a share, so copy issue is spread over the
 // four SM sub-partitions.
 template <int NDG>
-__global__ void __launch_bounds__(64 + 128 * NDG, 1)
+__global__ void __launch_bounds__(128 + 128 * NDG, 1)
     zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ PlaneMaps pm,
                    const __grid_constant__ CUtensorMap mmap, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = ptx::smem_addr(smem);
-    const uint32_t bar_full = sbase;                         // [2 * NDG]
-    const uint32_t bar_afull = sbase + 8 * kMaxStages;        // [kMaxABuffers]
+    const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
+    const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
+    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [kMaxABuffers]
     const uint32_t bar_aempty = bar_afull + 8 * kMaxABuffers;
     const uint32_t bar_xfull = bar_aempty + 8 * kMaxABuffers;  // [kMaxX]
     const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
@@ -101,7 +99,10 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
     const SlotLayout L = p.slot;
 
     if (tid == 0) {
-        for (int s = 0; s < 2 * NDG; ++s) ptx::mbar_init(bar_addr(bar_full, s), 1);
+        for (int s = 0; s < 2 * NDG; ++s) {
+            ptx::mbar_init(bar_addr(bar_full, s), 1);
+            ptx::mbar_init(bar_addr(bar_free, s), 4);
+        }
         for (int i = 0; i < kMaxX; ++i) {
             ptx::mbar_init(bar_addr(bar_xfull, i), 1);
             ptx::mbar_init(bar_addr(bar_xempty, i), 1);
@@ -192,53 +193,55 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
                 ptx::mbar_wait(bar_addr(bar_xfull, k % nx), (k / nx) & 1);
         }
         __syncwarp();
-    } else {
-        // ------------------------------------------------------ decoders
-        const int dw = warp - 1, g = dw >> 2;
-        const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
-        const int tau = lane >> 4;
-        const bool valid = tau == 0 || has1;
+    } else if (warp >= 4 * NDG + 2) {
+        // ------------------------------------------------------ producers
+        // Producer pi fills the compressed slots of slices pi, pi + 2, ...
+        // (slice k goes to group k % NDG, slot 2 * group + ((k / NDG) & 1))
+        // once the group has released the slot's previous contents. Per
+        // slot: one 4-D tensor load for the three bitmap planes of both tile
+        // rows, one 3-D load for the band offsets and one bulk copy per
+        // payload run, all completing on the slot's barrier.
+        const int pi = warp - (4 * NDG + 2);
         const int2* goffs = reinterpret_cast<const int2*>(p.global);
         const uint64_t pol_w = ptx::policy_evict_first();
-        RowDecoder<8 * 128 * NDG> dec;
-        dec.init(tables, sbase + p.off_rb + uint32_t(dw * 32 + lane) * 8u, lane, q, p.start_exp);
-        const uint32_t trow = tmem + (uint32_t(32 * q) << 16) + p.a_col0;
-
-        // Lanes 0-3 hold the (common, rare) offsets of the group's u-th slice:
-        // lane 2*t + e = entry e (0 start, 1 end) of tile row t.
-        auto load_offsets = [&](int u) {
-            const int k = g + u * NDG;
+        // Lanes 0-3 hold the (common, rare) offsets of slice k: lane 2*t + e
+        // = entry e (0 start, 1 end) of tile row t.
+        auto load_offsets = [&](int k) {
             int2 v = make_int2(0, 0);
             if (k < nk && lane < 4 && ((lane >> 1) == 0 || has1))
                 v = goffs[size_t(tr0 + (lane >> 1)) * p.kt + kt0 + k + (lane & 1)];
             return v;
         };
-        // Fill buffer b with the group's u-th slice (its offsets in `o`).
-        auto issue = [&](int u, int b, int2 o) {
-            const int k = g + u * NDG;
+        int2 o = load_offsets(pi);
+        bool ok = true;
+        int last = -1;  // last slice issued
+        for (int k = pi; k < nk; k += 2) {
+            const int2 onext = load_offsets(k + 2);
+            const int g = k % NDG, u = k / NDG, sidx = g * 2 + (u & 1);
             int2 e[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 e[i].x = __shfl_sync(kFullMask, o.x, i), e[i].y = __shfl_sync(kFullMask, o.y, i);
-            uint32_t clen[2], rlen[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                const int2 st = e[2 * t], en = e[2 * t + 1];
-                const bool live = t == 0 || has1;
-                // Payload copies need 16-byte aligned sources, which the
-                // offsets of valid packed data always give.
-                clen[t] = live && (st.x & 15) == 0
-                              ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
-                              : 0u;
-                rlen[t] = live && (st.y & 7) == 0
-                              ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
-                              : 0u;
-            }
             if (lane == 0) {
-                const uint32_t slot = sbase + p.off_slots + uint32_t(g * 2 + b) * L.bytes;
-                const uint32_t full = bar_addr(bar_full, g * 2 + b);
-                const int kc = kt0 + k;
-                if (q == 1) {
+                if (u >= 2) ok = ptx::mbar_wait(bar_addr(bar_free, sidx), ((u >> 1) - 1) & 1);
+                if (ok) {
+                    uint32_t clen[2], rlen[2];
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const int2 st = e[2 * t], en = e[2 * t + 1];
+                        const bool live = t == 0 || has1;
+                        // Payload copies need 16-byte aligned sources, which
+                        // the offsets of valid packed data always give.
+                        clen[t] = live && (st.x & 15) == 0
+                                      ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
+                                      : 0u;
+                        rlen[t] = live && (st.y & 7) == 0
+                                      ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
+                                      : 0u;
+                    }
+                    const uint32_t slot = sbase + p.off_slots + uint32_t(sidx) * L.bytes;
+                    const uint32_t full = bar_addr(bar_full, sidx);
+                    const int kc = kt0 + k;
                     ptx::mbar_arrive_expect_tx(full, p.plane_box_bytes + 64u + clen[0] + clen[1] +
                                                          rlen[0] + rlen[1]);
                     if (pm.count == 1) {
@@ -246,76 +249,71 @@ __global__ void __launch_bounds__(64 + 128 * NDG, 1)
                     } else {
 #pragma unroll
                         for (int i = 0; i < 3; ++i)
-                            ptx::tma_load_3d(slot + uint32_t(i) * L.plane_stride, &pm.map[i], 0, kc,
-                                             tr0, full, pol_w);
+                            ptx::tma_load_3d(slot + uint32_t(i) * L.plane_stride, &pm.map[i], 0,
+                                             kc, tr0, full, pol_w);
                     }
-                } else if (q == 2) {
                     ptx::tma_load_3d(slot + L.med, &mmap, 0, kc, tr0, full, pol_w);
                     if (clen[0]) ptx::bulk_g2s(slot + L.common0, p.sm + e[0].x, clen[0], full, pol_w);
-                } else if (q == 3) {
                     if (clen[1]) ptx::bulk_g2s(slot + L.common1, p.sm + e[2].x, clen[1], full, pol_w);
-                } else {
                     if (rlen[0]) ptx::bulk_g2s(slot + L.rare0, p.rare + e[0].y, rlen[0], full, pol_w);
                     if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[2].y, rlen[1], full, pol_w);
+                    last = k;
                 }
             }
-        };
-
-        const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
-        {
-            const int2 o0 = load_offsets(0), o1 = load_offsets(1);
-            if (nu > 0) issue(0, 0, o0);
-            if (nu > 1) issue(1, 1, o1);
+            if (!__shfl_sync(kFullMask, ok, 0)) break;
+            o = onext;
         }
-        int2 onext = load_offsets(2);
+        // Never leave copies in flight: wait (bounded) for the last use of
+        // every slot this producer filled.
+        if (lane == 0)
+            for (int k = max(pi, last - 2 * NDG + 2); k >= 0 && k <= last; k += 2) {
+                const int g = k % NDG, u = k / NDG;
+                ptx::mbar_wait(bar_addr(bar_full, g * 2 + (u & 1)), (u >> 1) & 1);
+            }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------ decoders
+        const int dw = warp - 1, g = dw >> 2;
+        const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
+        const int tau = lane >> 4;
+        const bool valid = tau == 0 || has1;
+        RowDecoder<8 * 128 * NDG> dec;
+        dec.init(tables, sbase + p.off_rb + uint32_t(dw * 32 + lane) * 8u, lane, q, p.start_exp);
+        const uint32_t trow = tmem + (uint32_t(32 * q) << 16) + p.a_col0;
+        const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
         uint32_t out[32];
         bool ok = ptx::mbar_wait(bar_tab, 0);
-        int waited = 0;  // uses whose slot this warp saw land
         for (int u = 0; u < nu; ++u) {
-            const int b = u & 1;
-            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(g * 2 + b) * L.bytes);
-            ok = ok && ptx::mbar_wait(bar_addr(bar_full, g * 2 + b), (u >> 1) & 1);
-            ok = __all_sync(kFullMask, ok);
-            if (ok) {
-                waited = u + 1;
-                dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
-                           slot + L.med + uint32_t(tau) * 32u,
-                           slot + (tau ? L.common1 : L.common0),
-                           slot + (tau ? L.rare1 : L.rare0), cap_c, cap_r, out);
-                if (!valid) {
+            const int sidx = g * 2 + (u & 1);
+            const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
+            ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), (u >> 1) & 1);
+            if (!__all_sync(kFullMask, ok)) break;
+            dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
+                       slot + L.med + uint32_t(tau) * 32u, slot + (tau ? L.common1 : L.common0),
+                       slot + (tau ? L.rare1 : L.rare0), cap_c, cap_r, out);
+            // The slot's bytes are in registers now: release it to the producer.
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_free, sidx));
+            if (!valid) {
 #pragma unroll
-                    for (int w = 0; w < 32; ++w) out[w] = 0;
-                }
-                // The A buffer is free once the MMAs of its previous use finished.
-                const int a = 2 * g + (u & 1), ause = u >> 1;
-                if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
-                ok = __all_sync(kFullMask, ok);
-                if (ok) {
-                    ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
-                    ptx::tmem_wait_st();
-                    ptx::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) ptx::mbar_arrive(bar_addr(bar_afull, a));
-                }
+                for (int w = 0; w < 32; ++w) out[w] = 0;
             }
-            // Every warp of the group passes here once per slice, failed or
-            // not: after it the group's reads of buffer b are over.
-            named_sync(1 + g, 128);
-            if (ok && u + 2 < nu) issue(u + 2, b, onext);
-            onext = load_offsets(u + 3);
+            // The A buffer is free once the MMAs of its previous use finished.
+            const int a = 2 * g + (u & 1), ause = u >> 1;
+            if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
+            if (!__all_sync(kFullMask, ok)) break;
+            ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
+            ptx::tmem_wait_st();
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_afull, a));
         }
-        // Never leave copies in flight: after a failure, wait (bounded) for
-        // the slots this warp issued into but did not see land.
-        if (!ok && lane == 0)
-            for (int u = waited; u < min(nu, waited + 2); ++u)
-                ptx::mbar_wait(bar_addr(bar_full, g * 2 + (u & 1)), (u >> 1) & 1);
-        __syncwarp();
     }
 
     // ---------------------------------------------------------- epilogue
     float* red = reinterpret_cast<float*>(smem + p.off_x);  // [bn][128] FP32 when S > 1
     if (warp >= 1 && warp <= 4 * NDG) {
-        const int dw = warp - 1, g = dw >> 2, q = warp & 3;
+        const int g = (warp - 1) >> 2, q = warp & 3;
         const bool dok = ptx::mbar_wait(bar_d, 0);
         ptx::tc_fence_after();
         const int row = 32 * q + lane;  // TMEM lane = slot in the reduction tile
