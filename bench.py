@@ -264,6 +264,11 @@ def run_ours(args, world: int, rank: int) -> dict | None:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # A kernel wait that gave up (bounded waits raise a device flag) makes the
+    # numbers meaningless: fail loudly instead of printing them.
+    flags = runtime.device_flags()
+    if flags:
+        raise SystemExit(f"device failure flags {flags:#x} set during the benchmark")
     zip_total, dense_total, e2e_total = agg(zip_ms), agg(dense_ms), agg(e2e_ms)
     bytes_all = torch.tensor([float(total_bytes)], dtype=torch.float64, device=dev)
     if world > 1:

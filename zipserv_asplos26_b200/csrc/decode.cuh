@@ -19,8 +19,10 @@
 //     elements (nibble-wise prefix sum), which is the byte-permute selector
 //     that spreads the compact payload bytes to their positions;
 //   * the compact common payload bytes come from one funnel-shift pair;
-//   * exponents come from two 8-byte palettes (low byte bit 7 = exponent LSB,
-//     high byte bits 0-6 = exponent >> 1) indexed by the code nibbles;
+//   * exponents come from one 8-byte palette indexed by the code nibbles,
+//     holding each exponent rotated right by one bit: bit 7 (exponent LSB)
+//     is what the low byte takes, bits 0-6 (exponent >> 1) what the high
+//     byte takes, so one byte permute serves both byte planes;
 //   * rare words are scattered into a per-thread row buffer by one loop over
 //     the row's rare bits (not per segment) and merged with a byte permute.
 // Reference decoder semantics: csrc/L_Kernel.cuh:146-250 and :1022-1143;
@@ -81,7 +83,10 @@ struct RowDecoder {
     int band;            // 16-row band inside the tile
     uint32_t lane16;     // lane inside the 16-lane half
     uint32_t row_elems;  // 64*rt + 8*r: elements before this row in its small-tile pair
-    uint32_t lp_lo, lp_hi, hp_lo, hp_hi;  // exponent palettes, indexed by code
+    // Exponent palette indexed by code: byte c = exponent rotated right by one
+    // bit (bit 7 = exponent bit 0, bits 0-6 = exponent >> 1), i.e. exactly the
+    // bits a common element's low byte and high byte take from it.
+    uint32_t xp_lo, xp_hi;
     // Multipliers kept in registers so address and selector arithmetic runs
     // as IMAD on the FMA pipe instead of shifts on the integer ALU pipe.
     uint32_t k2, k4, k8, k128, krank, kneg4, khi, kstride;
@@ -98,13 +103,12 @@ struct RowDecoder {
         bm_word = (band * 16 + rt) * 2 + (r >> 2);
         lane16 = uint32_t(lane) & 15u;
         row_elems = uint32_t(64 * rt + 8 * r);
-        uint32_t lp[2] = {0, 0}, hp[2] = {0, 0};
+        uint32_t xp[2] = {0, 0};
         for (int c = 1; c < 8; ++c) {
             const uint32_t e = (start_exp + uint32_t(c)) & 255u;
-            lp[c >> 2] |= ((e & 1u) << 7) << (8 * (c & 3));
-            hp[c >> 2] |= (e >> 1) << (8 * (c & 3));
+            xp[c >> 2] |= (((e & 1u) << 7) | (e >> 1)) << (8 * (c & 3));
         }
-        lp_lo = lp[0], lp_hi = lp[1], hp_lo = hp[0], hp_hi = hp[1];
+        xp_lo = xp[0], xp_hi = xp[1];
         k2 = ptx::launder(2u);
         k4 = ptx::launder(4u);
         k8 = ptx::launder(8u);
@@ -226,8 +230,9 @@ struct RowDecoder {
             const uint32_t cj = code[j];
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank);
-                uint32_t a = (pe & 0x7F7F7F7Fu) | __byte_perm(lp_lo, lp_hi, cj);
-                uint32_t b = (pe & 0x80808080u) | __byte_perm(hp_lo, hp_hi, cj);
+                const uint32_t xv = __byte_perm(xp_lo, xp_hi, cj);
+                uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
+                uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 a = __byte_perm(a, rl.x, mix);
                 b = __byte_perm(b, rh.x, mix);
                 out[4 * j] = __byte_perm(a, b, 0x5140);
@@ -236,8 +241,9 @@ struct RowDecoder {
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank_hi);
                 const uint32_t ch = ptx::mul_hi(cj, khi);
-                uint32_t a = (pe & 0x7F7F7F7Fu) | __byte_perm(lp_lo, lp_hi, ch);
-                uint32_t b = (pe & 0x80808080u) | __byte_perm(hp_lo, hp_hi, ch);
+                const uint32_t xv = __byte_perm(xp_lo, xp_hi, ch);
+                uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
+                uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 a = __byte_perm(a, rl.y, mix_hi);
                 b = __byte_perm(b, rh.y, mix_hi);
                 out[4 * j + 2] = __byte_perm(a, b, 0x5140);

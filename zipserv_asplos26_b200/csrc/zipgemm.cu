@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
-        // Slice k = NDG*u + g comes from group g's A buffer 2g + (u & 1)
+        // Slice k = NDG*u + g comes from group g's A buffer g + NDG*(u & 1)
         // (use u >> 1) and x slot k % nx. The loop keeps every index as a
         // counter: this thread shares its sub-partition with decoder warps,
         // so each instruction here costs several issue cycles.
@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
             const uint32_t abase = tmem + p.a_col0;
             const int nx = p.nx;
+            const bool xmerged = nx == 2 * NDG;
             int xs = 0;
             uint32_t xph = 0;
             bool ok = true;
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 #pragma unroll
                 for (int g = 0; g < NDG; ++g) {
                     if (k >= nk) break;
-                    const int a = 2 * g + (u & 1);
+                    const int a = g + NDG * (u & 1);  // == k % (2 * NDG)
                     if (!ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) ||
                         !ptx::mbar_wait(bar_addr(bar_afull, a), aph)) {
                         ok = false;
@@ -163,8 +164,10 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         ptx::mma_bf16_ts(tmem, at + 8u * kk, bdesc + 2u * kk, idesc, (k | kk) != 0);
+                    // With nx == 2 * NDG the x slot is the A buffer's index
+                    // and one commit frees both.
                     ptx::mma_commit(bar_addr(bar_aempty, a));
-                    ptx::mma_commit(bar_addr(bar_xempty, xs));
+                    if (!xmerged) ptx::mma_commit(bar_addr(bar_xempty, xs));
                     if (++xs == nx) xs = 0, xph ^= 1u;
                     ++k;
                 }
@@ -182,7 +185,8 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             int issued = 0;
             for (int k = 0; k < nk; ++k) {
                 const int xs = k % nx;
-                if (k >= nx && !ptx::mbar_wait(bar_addr(bar_xempty, xs), ((k / nx) - 1) & 1)) break;
+                const uint32_t freed = nx == 2 * NDG ? bar_aempty : bar_xempty;
+                if (k >= nx && !ptx::mbar_wait(bar_addr(freed, xs), ((k / nx) - 1) & 1)) break;
                 ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
                 ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0,
                                  nblk * p.bn, kt0 + k, bar_addr(bar_xfull, xs), pol_x);
@@ -299,7 +303,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
                 for (int w = 0; w < 32; ++w) out[w] = 0;
             }
             // The A buffer is free once the MMAs of its previous use finished.
-            const int a = 2 * g + (u & 1), ause = u >> 1;
+            const int a = g + NDG * (u & 1), ause = u >> 1;
             if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
             ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
@@ -441,7 +445,10 @@ GemmLayout gemm_layout(int ndg, int bn, uint32_t plane_pitch, uint32_t cap_c, ui
     const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
     const uint32_t used = l.off_x + slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    l.nx = std::min<int>(kMaxX, int(avail / l.x_bytes));
+    // More than two rounds of x slots (2 * ndg) buys nothing: the MMAs
+    // trail the decoders by less than that. At exactly 2 * ndg an x slot is
+    // freed by the same commit as the A buffer of its slice.
+    l.nx = std::min<int>({kMaxX, 2 * ndg, int(avail / l.x_bytes)});
     l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
     l.total = l.off_slots + slots + kRingPadBytes;
     return l;
