@@ -23,8 +23,10 @@
 //     holding each exponent rotated right by one bit: bit 7 (exponent LSB)
 //     is what the low byte takes, bits 0-6 (exponent >> 1) what the high
 //     byte takes, so one byte permute serves both byte planes;
-//   * rare words are scattered into a per-thread row buffer by one loop over
-//     the row's rare bits (not per segment) and merged with a byte permute.
+//   * the row is written with eight 16-byte stores into a 128-byte-swizzled
+//     tile row (the layout the tensor cores and TMA stores read), then one
+//     loop over the row's rare bits patches each rare element with one
+//     16-bit store: the common-element arithmetic never looks at rares.
 // Reference decoder semantics: csrc/L_Kernel.cuh:146-250 and :1022-1143;
 // bit-exact results are checked against oracle/oracle.c:oracle_decode.
 #pragma once
@@ -37,11 +39,6 @@ namespace zs {
 constexpr uint32_t kFullMask = 0xFFFFFFFFu;
 constexpr int kCodeTableBytes = 256 * 32 * 4;  // per bitmap byte x per lane
 constexpr int kTableBytes = kCodeTableBytes;
-// Row buffer: per decoder thread 16 chunks of 8 bytes (low bytes of the rare
-// words of segments 0-7, then their high bytes). Chunk c of thread t lives at
-// c * stride + 8 * t, stride = 8 * (decoder threads): conflict-free 8-byte
-// loads at immediate offsets.
-constexpr int kRowBufferBytes = 128;
 // Bytes of readable shared memory required after the slot ring: payload
 // reads are not clamped per row segment and may run past a corrupted tile.
 constexpr int kRingPadBytes = 2048;
@@ -73,11 +70,15 @@ __host__ __device__ constexpr uint32_t common_capacity(int max_common) {
 __device__ const DecodeTables g_decode_tables alignas(16) = make_decode_tables();
 
 // --------------------------------------------------------------- decoder
-// RBSTRIDE: byte distance between row-buffer chunks (8 * decoder threads).
-template <int RBSTRIDE>
+// What decode() leaves for store(): where each segment's rare words start
+// (16 bits per segment) and which positions are rare.
+struct RareState {
+    uint32_t ro[4];    // segment 2h in bits 0-15, segment 2h+1 in bits 16-31
+    uint32_t i03, i47;  // bitmap OR of segments 0-3 / 4-7 (bit set = common)
+};
+
 struct RowDecoder {
     uint32_t ct;         // shared address of code table + lane*4
-    uint32_t rbs;        // shared address of this thread's chunk-0 row-buffer bytes
     uint32_t selr;       // byte-permute selector: byte (r & 3) of a, zeros elsewhere
     int bm_word;         // u32 index of this row's bitmap word inside one plane
     int band;            // 16-row band inside the tile
@@ -89,16 +90,14 @@ struct RowDecoder {
     uint32_t xp_lo, xp_hi;
     // Multipliers kept in registers so address and selector arithmetic runs
     // as IMAD on the FMA pipe instead of shifts on the integer ALU pipe.
-    uint32_t k2, k4, k8, k128, krank, kneg4, khi, kstride;
+    uint32_t k2, k4, k8, k128, krank, khi;
 
     // The warp decodes band `band_` of both tiles; lane = tau*16 + rt*8 + r.
-    // row_buffer is the shared address of this thread's chunk 0.
-    __device__ __forceinline__ void init(uint32_t tables_smem, uint32_t row_buffer, int lane,
-                                         int band_, uint32_t start_exp) {
+    __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int band_,
+                                         uint32_t start_exp) {
         const int r = lane & 7, rt = (lane >> 3) & 1;
         band = band_;
         ct = tables_smem + uint32_t(lane) * 4u;
-        rbs = row_buffer;
         selr = uint32_t(r & 3) | 0x4440u;
         bm_word = (band * 16 + rt) * 2 + (r >> 2);
         lane16 = uint32_t(lane) & 15u;
@@ -114,21 +113,21 @@ struct RowDecoder {
         k8 = ptx::launder(8u);
         k128 = ptx::launder(128u);
         krank = ptx::launder(0x11111110u);
-        kneg4 = ptx::launder(0xFFFFFFFCu);
         khi = ptx::launder(0x10000u);
-        kstride = ptx::launder(uint32_t(RBSTRIDE));
     }
 
     // Decode this thread's row of one 64x64 tile whose data sits in shared
     // memory at: `plane` (bitmap1; bitmap2/3 follow at +plane_stride,
     // +2*plane_stride), `medium` (the tile's four band offset pairs),
-    // `common` / `rare` (the tile's payloads). All 32 lanes of the warp must
-    // call this together (lanes 0-15 and 16-31 may pass different tiles).
-    // cap_c / cap_r (bytes / words) bound the band offsets and every rare
-    // index; payload reads stay within kRingPadBytes past the tile's data.
+    // `common` (the tile's common payload). All 32 lanes of the warp must call
+    // this together (lanes 0-15 and 16-31 may pass different tiles). out[]
+    // receives the row with every common element in place and don't-care
+    // bits at rare positions; store() writes it out and patches the rare
+    // words. cap_c / cap_r (bytes / words) bound the band offsets; payload
+    // reads stay within kRingPadBytes past the tile's data.
     __device__ __forceinline__ void decode(uint32_t plane, uint32_t plane_stride, uint32_t medium,
-                                           uint32_t common, uint32_t rare, uint32_t cap_c,
-                                           uint32_t cap_r, uint32_t (&out)[32]) const {
+                                           uint32_t common, uint32_t cap_c, uint32_t cap_r,
+                                           uint32_t (&out)[32], RareState& rs) const {
         plane += uint32_t(bm_word) * 4u;
         const int2 med = ptx::lds_s64(medium + uint32_t(band) * 8u);
         uint32_t code[8], flag[8], ind[8];
@@ -145,8 +144,8 @@ struct RowDecoder {
             flag[j] = t1 | t2 | t3;  // nibble p = 1 when position p is common
             ind[j] = m1 | m2 | m3;
             const uint32_t cnt = __popc(ind[j]);
-            if (j < 4) k0 |= cnt << (8 * j);
-            else k1 |= cnt << (8 * (j - 4));
+            if (j < 4) k0 = ptx::mad_lo(cnt, 1u << (8 * j), k0);
+            else k1 = ptx::mad_lo(cnt, 1u << (8 * (j - 4)), k1);
         }
         // Inclusive 16-lane scan of the byte-packed row counts (a pair of
         // small tiles holds at most 128 common elements: bytes never carry).
@@ -171,44 +170,16 @@ struct RowDecoder {
             run += __byte_perm(tot, 0, 0x4440 | (j & 3));
         }
         // Rare words: segment j's run starts at rbase + (elements before the
-        // row segment in the band) - (common elements before it). One loop
-        // over the row's rare bits scatters them into the row buffer; the
-        // per-segment starts and masks stay in registers, indexed by byte
-        // permutes.
-        {
-            const uint32_t rconst = rbase + cb + row_elems;
-            uint32_t ro[4];
+        // row segment in the band) - (common elements before it).
+        const uint32_t rconst = rbase + cb + row_elems;
 #pragma unroll
-            for (int h = 0; h < 4; ++h)
-                ro[h] = __byte_perm(rconst + 128u * (2 * h) - off[2 * h],
-                                    rconst + 128u * (2 * h + 1) - off[2 * h + 1], 0x5410);
-            const uint32_t i03 = __byte_perm(__byte_perm(ind[0], ind[1], 0x0040),
-                                             __byte_perm(ind[2], ind[3], 0x0040), 0x5410);
-            const uint32_t i47 = __byte_perm(__byte_perm(ind[4], ind[5], 0x0040),
-                                             __byte_perm(ind[6], ind[7], 0x0040), 0x5410);
-            uint32_t rlo = ~i03, rhi = ~i47;
-            const uint32_t rcap = cap_r ? cap_r - 1 : 0;
-            while (rlo | rhi) {
-                uint32_t p;
-                if (rlo) {
-                    p = __ffs(rlo) - 1;
-                    rlo &= rlo - 1;
-                } else {
-                    p = 31 + __ffs(rhi);
-                    rhi &= rhi - 1;
-                }
-                const uint32_t j = p >> 3, c = p & 7;
-                const uint32_t seg_ind = __byte_perm(i03, i47, j);  // byte j
-                const uint32_t pair = (j >> 1) < 2 ? __byte_perm(ro[0], ro[1], (j & 2) ? 0x7654 : 0x3210)
-                                                   : __byte_perm(ro[2], ro[3], (j & 2) ? 0x7654 : 0x3210);
-                const uint32_t base = (j & 1) ? (pair >> 16) : (pair & 0xFFFFu);
-                const uint32_t idx = base + c - __popc(seg_ind & 0xFFu & ((1u << c) - 1u));
-                const uint32_t word = ptx::lds_u16(rare + 2u * min(idx & 0xFFFFu, rcap));
-                const uint32_t at = ptx::mad_lo(j, kstride, rbs + c);
-                ptx::sts8(at, word);
-                ptx::sts8(at + 8u * RBSTRIDE, word >> 8);
-            }
-        }
+        for (int h = 0; h < 4; ++h)
+            rs.ro[h] = __byte_perm(rconst + 128u * (2 * h) - off[2 * h],
+                                   rconst + 128u * (2 * h + 1) - off[2 * h + 1], 0x5410);
+        rs.i03 = __byte_perm(__byte_perm(ind[0], ind[1], 0x0040),
+                             __byte_perm(ind[2], ind[3], 0x0040), 0x5410);
+        rs.i47 = __byte_perm(__byte_perm(ind[4], ind[5], 0x0040),
+                             __byte_perm(ind[6], ind[7], 0x0040), 0x5410);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t co = off[j];
@@ -217,38 +188,62 @@ struct RowDecoder {
             const uint32_t sh = ptx::mad_lo(co, k8, 0);
             const uint32_t q0 = __funnelshift_r(w0, w1, sh);
             const uint32_t q1 = __funnelshift_r(w1, w2, sh);
-            // Nibble p of `rank` = number of common positions before p; nibble
-            // p of `mix` = p&3 when common (decoded byte), 4+(p&3) when rare
-            // (row-buffer byte): 0x76547654 - 4*flag.
-            const uint32_t f = flag[j];
-            const uint32_t rank = ptx::mad_lo(f, krank, 0);
-            const uint32_t mix = ptx::mad_lo(f, kneg4, 0x76547654u);
+            // Nibble p of `rank` = number of common positions before p: the
+            // byte-permute selector that spreads the compact payload bytes.
+            const uint32_t rank = ptx::mad_lo(flag[j], krank, 0);
             const uint32_t rank_hi = ptx::mul_hi(rank, khi);
-            const uint32_t mix_hi = ptx::mul_hi(mix, khi);
-            const uint2 rl = ptx::lds_v64(rbs + uint32_t(j) * RBSTRIDE);
-            const uint2 rh = ptx::lds_v64(rbs + uint32_t(8 + j) * RBSTRIDE);
             const uint32_t cj = code[j];
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank);
                 const uint32_t xv = __byte_perm(xp_lo, xp_hi, cj);
-                uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
-                uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
-                a = __byte_perm(a, rl.x, mix);
-                b = __byte_perm(b, rh.x, mix);
+                const uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
+                const uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 out[4 * j] = __byte_perm(a, b, 0x5140);
                 out[4 * j + 1] = __byte_perm(a, b, 0x7362);
             }
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank_hi);
-                const uint32_t ch = ptx::mul_hi(cj, khi);
-                const uint32_t xv = __byte_perm(xp_lo, xp_hi, ch);
-                uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
-                uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
-                a = __byte_perm(a, rl.y, mix_hi);
-                b = __byte_perm(b, rh.y, mix_hi);
+                const uint32_t xv = __byte_perm(xp_lo, xp_hi, ptx::mul_hi(cj, khi));
+                const uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
+                const uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 out[4 * j + 2] = __byte_perm(a, b, 0x5140);
                 out[4 * j + 3] = __byte_perm(a, b, 0x7362);
             }
+        }
+    }
+
+    // Write a decoded row into a 128-byte row of a tile in the 128-byte
+    // swizzled layout (16-byte chunk c at (c ^ (row & 7)) * 16; `swz` =
+    // (row & 7) << 4), then overwrite its rare elements with their words from
+    // `rare` (indices clamped below cap_r). Pass all_common = true for a row
+    // that must not be patched.
+    __device__ __forceinline__ void store(uint32_t row, uint32_t swz, const uint32_t (&out)[32],
+                                          const RareState& rs, uint32_t rare, uint32_t cap_r,
+                                          bool all_common) const {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            ptx::sts128(row + ((uint32_t(c) << 4) ^ swz),
+                        make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]));
+        uint32_t rlo = all_common ? 0u : ~rs.i03, rhi = all_common ? 0u : ~rs.i47;
+        const uint32_t rcap = cap_r ? cap_r - 1 : 0;
+        while (rlo | rhi) {
+            uint32_t p;
+            if (rlo) {
+                p = __ffs(rlo) - 1;
+                rlo &= rlo - 1;
+            } else {
+                p = 31 + __ffs(rhi);
+                rhi &= rhi - 1;
+            }
+            const uint32_t j = p >> 3, c = p & 7;
+            const uint32_t seg_ind = __byte_perm(rs.i03, rs.i47, j);  // byte j
+            const uint32_t pair = (j >> 1) < 2
+                                      ? __byte_perm(rs.ro[0], rs.ro[1], (j & 2) ? 0x7654 : 0x3210)
+                                      : __byte_perm(rs.ro[2], rs.ro[3], (j & 2) ? 0x7654 : 0x3210);
+            const uint32_t base = (j & 1) ? (pair >> 16) : (pair & 0xFFFFu);
+            const uint32_t idx = base + c - __popc(seg_ind & 0xFFu & ((1u << c) - 1u));
+            const uint32_t word = ptx::lds_u16(rare + 2u * min(idx & 0xFFFFu, rcap));
+            ptx::sts16(row + (((j << 4) ^ swz) | (c << 1)), word);
         }
     }
 };

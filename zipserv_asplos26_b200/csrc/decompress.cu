@@ -152,10 +152,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // is tile j of each half (lanes 0-15: half 0, lanes 16-31: half 1).
         const int dw = warp - 1, g = dw >> 2, q = dw & 3;
         const int tau = lane >> 4;
-        RowDecoder<8 * 128 * kDecGroups> dec;
-        dec.init(tables, sbase + p.off_rb + uint32_t(dw * 32 + lane) * 8u, lane, q, p.start_exp);
+        RowDecoder dec;
+        dec.init(tables, lane, q, p.start_exp);
         const uint32_t obuf = sbase + p.off_out + uint32_t(dw) * 2 * kOutTileBytes;
         uint32_t out[32];
+        RareState rs;
         int nstore = 0;
         bool ok = ptx::mbar_wait(bar_tab, 0);
         for (int it = g; it < nlocal; it += kDecGroups) {
@@ -171,17 +172,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             for (int j = 0; j < n0; ++j) {
                 const int2 hdr = ptx::lds_s64(slot + L.hdr + uint32_t(tau * kMaxGroup + j) * 8u);
                 dec.decode(plane + 512u * uint32_t(j), L.plane_stride, med + 32u * uint32_t(j),
-                           com + uint32_t(hdr.x), slot + L.rare0 + 2u * uint32_t(hdr.y), cap_c,
-                           cap_r, out);
+                           com + uint32_t(hdr.x), cap_c, cap_r, out, rs);
                 // Stage the warp's 32 rows: row `lane`, 16-byte chunk c at
-                // position c ^ (row & 7) (the TMA 128-byte swizzle).
+                // position c ^ (row & 7) (the TMA 128-byte swizzle); rare
+                // elements are patched in place. A missing second tile is
+                // staged but never stored.
                 const uint32_t buf = obuf + uint32_t(nstore & 1) * kOutTileBytes;
                 if (lane == 0) ptx::bulk_wait_read<1>();
                 __syncwarp();
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    ptx::sts128(buf + uint32_t(lane) * 128 + ((uint32_t(c) ^ (lane & 7)) << 4),
-                                make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]));
+                dec.store(buf + uint32_t(lane) * 128u, uint32_t(lane & 7) << 4, out, rs,
+                          slot + L.rare0 + 2u * uint32_t(hdr.y), cap_r, tau == 1 && j >= n1);
                 ptx::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -227,8 +227,7 @@ cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* r
     p.cap_c = common_capacity(max_common);
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
-    p.off_rb = kBarrierBytes + kTableBytes;
-    p.off_out = round_up_u(p.off_rb + 128 * kDecGroups * kRowBufferBytes, 1024);
+    p.off_out = round_up_u(kBarrierBytes + kTableBytes, 1024);
     p.off_slots = p.off_out + 4 * kDecGroups * 2 * kOutTileBytes;
     const uint32_t used = p.off_slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_optin) > used ? uint32_t(smem_optin) - used : 0;

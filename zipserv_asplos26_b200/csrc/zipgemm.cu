@@ -5,17 +5,18 @@
 // One CTA computes a 128-row block of W (two vertically adjacent 64x64 global
 // tiles) against a tile of up to 256 tokens over a contiguous range of 64-wide
 // K slices. Warp roles (1 CTA per SM):
-//   warp 0      allocates tensor memory; lane 0 issues tcgen05.mma
-//               (A = decoded W slice read from TMEM, B = x tile from shared
-//               memory, 128-byte swizzle, D = FP32 accumulator in TMEM);
+//   warp 0      allocates tensor memory; lane 0 issues tcgen05.mma with
+//               both operands in shared memory (A = a decoder group's tile
+//               of decoded W, B = an x tile, both 128-byte swizzled) and the
+//               FP32 accumulator in TMEM;
 //   warps 1..   NDG decoder groups of four warps. Group g decodes K slices
 //               g, g+NDG, ... from two compressed slots it owns: while it
 //               decodes one, the other is filling. Warp w decodes 16-row
-//               band w%4 of both tiles (row = tile*64 + 16*band + i, TMEM
-//               lane = 32*band + 16*tile + i); each thread rebuilds one W row
-//               (64 BF16) per slice and stores it with tcgen05.st into one of
-//               the group's two TMEM A buffers, so decoded weights never
-//               touch shared memory;
+//               band w%4 of both tiles (row = tile*64 + 16*band + i, tile
+//               row = 32*band + 16*tile + i); each thread rebuilds one W row
+//               (64 BF16) per slice in registers, writes it into the group's
+//               A tile with eight 16-byte stores and patches its rare
+//               elements with 16-bit stores;
 //   next warp   keeps an x ring of nx slices filled with 3-D TMA loads;
 //   last two    producers: fill the groups' slots as soon as a group releases
 //               one, with few, large copies (an SM's copy engine takes ~100
@@ -79,9 +80,9 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
     const uint32_t sbase = ptx::smem_addr(smem);
     const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
     const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
-    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [kMaxABuffers]
-    const uint32_t bar_aempty = bar_afull + 8 * kMaxABuffers;
-    const uint32_t bar_xfull = bar_aempty + 8 * kMaxABuffers;  // [kMaxX]
+    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [NDG] group's A tile written
+    const uint32_t bar_aempty = bar_afull + 8 * kMaxGroups;   // [NDG] A tile read by the MMAs
+    const uint32_t bar_xfull = bar_aempty + 8 * kMaxGroups;   // [kMaxX]
     const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
     const uint32_t bar_d = bar_xempty + 8 * kMaxX;
     const uint32_t bar_tab = bar_d + 8;
@@ -107,9 +108,9 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             ptx::mbar_init(bar_addr(bar_xfull, i), 1);
             ptx::mbar_init(bar_addr(bar_xempty, i), 1);
         }
-        for (int i = 0; i < kMaxABuffers; ++i) {
-            ptx::mbar_init(bar_addr(bar_afull, i), 4);
-            ptx::mbar_init(bar_addr(bar_aempty, i), 1);
+        for (int i = 0; i < NDG; ++i) {
+            ptx::mbar_init(bar_addr(bar_afull, i), 4);   // the group's four warps
+            ptx::mbar_init(bar_addr(bar_aempty, i), 1);  // MMA commit
         }
         ptx::mbar_init(bar_d, 1);
         ptx::mbar_init(bar_tab, 1);
@@ -134,39 +135,37 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
-        // Slice k = NDG*u + g comes from group g's A buffer g + NDG*(u & 1)
-        // (use u >> 1) and x slot k % nx. The loop keeps every index as a
-        // counter: this thread shares its sub-partition with decoder warps,
-        // so each instruction here costs several issue cycles.
+        // Slice k = NDG*u + g: A = group g's shared-memory tile (use u),
+        // B = x slot k % nx. With nx == NDG the x slot is the group's index
+        // and one commit frees both. Indices are kept as counters: this
+        // thread shares its sub-partition with decoder warps.
         if (lane == 0) {
             const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
             const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
-            const uint32_t abase = tmem + p.a_col0;
+            const uint32_t abase = sbase + p.off_a;
             const int nx = p.nx;
-            const bool xmerged = nx == 2 * NDG;
+            const bool xmerged = nx == NDG;
             int xs = 0;
             uint32_t xph = 0;
             bool ok = true;
             for (int u = 0, k = 0; ok && k < nk; ++u) {
-                const uint32_t aph = uint32_t(u >> 1) & 1u;
+                const uint32_t aph = uint32_t(u) & 1u;
 #pragma unroll
                 for (int g = 0; g < NDG; ++g) {
                     if (k >= nk) break;
-                    const int a = g + NDG * (u & 1);  // == k % (2 * NDG)
                     if (!ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) ||
-                        !ptx::mbar_wait(bar_addr(bar_afull, a), aph)) {
+                        !ptx::mbar_wait(bar_addr(bar_afull, g), aph)) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
                     const uint64_t bdesc = ptx::smem_desc_sw128(xbase + uint32_t(xs) * xstep);
-                    const uint32_t at = abase + 32u * uint32_t(a);
+                    const uint64_t adesc = ptx::smem_desc_sw128(abase + uint32_t(g) * kATileBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        ptx::mma_bf16_ts(tmem, at + 8u * kk, bdesc + 2u * kk, idesc, (k | kk) != 0);
-                    // With nx == 2 * NDG the x slot is the A buffer's index
-                    // and one commit frees both.
-                    ptx::mma_commit(bar_addr(bar_aempty, a));
+                        ptx::mma_bf16_ss(tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                         (k | kk) != 0);
+                    ptx::mma_commit(bar_addr(bar_aempty, g));
                     if (!xmerged) ptx::mma_commit(bar_addr(bar_xempty, xs));
                     if (++xs == nx) xs = 0, xph ^= 1u;
                     ++k;
@@ -185,7 +184,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             int issued = 0;
             for (int k = 0; k < nk; ++k) {
                 const int xs = k % nx;
-                const uint32_t freed = nx == 2 * NDG ? bar_aempty : bar_xempty;
+                const uint32_t freed = nx == NDG ? bar_aempty : bar_xempty;
                 if (k >= nx && !ptx::mbar_wait(bar_addr(freed, xs), ((k / nx) - 1) & 1)) break;
                 ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
                 ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0,
@@ -281,11 +280,17 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
         const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
         const int tau = lane >> 4;
         const bool valid = tau == 0 || has1;
-        RowDecoder<8 * 128 * NDG> dec;
-        dec.init(tables, sbase + p.off_rb + uint32_t(dw * 32 + lane) * 8u, lane, q, p.start_exp);
-        const uint32_t trow = tmem + (uint32_t(32 * q) << 16) + p.a_col0;
+        RowDecoder dec;
+        dec.init(tables, lane, q, p.start_exp);
+        // This thread's row of the group's A tile: MMA row m = 32*q + lane
+        // (= accumulator lane), 128-byte swizzled.
+        const uint32_t m = uint32_t(32 * q + lane);
+        const uint32_t arow = sbase + p.off_a + uint32_t(g) * kATileBytes + (m >> 3) * 1024u +
+                              (m & 7u) * 128u;
+        const uint32_t swz = (m & 7u) << 4;
         const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
         uint32_t out[32];
+        RareState rs;
         bool ok = ptx::mbar_wait(bar_tab, 0);
         for (int u = 0; u < nu; ++u) {
             const int sidx = g * 2 + (u & 1);
@@ -294,28 +299,28 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             if (!__all_sync(kFullMask, ok)) break;
             dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
                        slot + L.med + uint32_t(tau) * 32u, slot + (tau ? L.common1 : L.common0),
-                       slot + (tau ? L.rare1 : L.rare0), cap_c, cap_r, out);
-            // The slot's bytes are in registers now: release it to the producer.
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_free, sidx));
+                       cap_c, cap_r, out, rs);
             if (!valid) {
 #pragma unroll
                 for (int w = 0; w < 32; ++w) out[w] = 0;
             }
-            // The A buffer is free once the MMAs of its previous use finished.
-            const int a = g + NDG * (u & 1), ause = u >> 1;
-            if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
+            // The A tile is free once the MMAs of the group's previous slice
+            // finished reading it.
+            if (u > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, g), (u - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
-            ptx::tmem_st_32x32b_x32(trow + 32u * a, out);
-            ptx::tmem_wait_st();
-            ptx::tc_fence_before();
+            dec.store(arow, swz, out, rs, slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
+            // Generic-proxy stores must be visible to the tensor cores.
+            ptx::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_afull, a));
+            if (lane == 0) {
+                ptx::mbar_arrive(bar_addr(bar_free, sidx));  // slot fully read
+                ptx::mbar_arrive(bar_addr(bar_afull, g));
+            }
         }
     }
 
     // ---------------------------------------------------------- epilogue
-    float* red = reinterpret_cast<float*>(smem + p.off_x);  // [bn][128] FP32 when S > 1
+    float* red = reinterpret_cast<float*>(smem + p.off_a);  // [bn][128] FP32 when S > 1
     if (warp >= 1 && warp <= 4 * NDG) {
         const int g = (warp - 1) >> 2, q = warp & 3;
         const bool dok = ptx::mbar_wait(bar_d, 0);
@@ -427,28 +432,27 @@ DeviceInfo& device_info(int device) {
 uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 struct GemmLayout {
-    uint32_t off_rb, off_x, off_slots, x_bytes, total;
+    uint32_t off_a, off_x, off_slots, x_bytes, total;
     SlotLayout slot;
     int nx;
 };
 
-// Shared memory: barriers | lookup tables | row buffers | x ring (1024-
-// aligned, nx slots of bn*128 bytes) | compressed slots (two per decoder
-// group) | pad. The x ring takes what the rest leaves, up to kMaxX slots.
+// Shared memory: barriers | lookup tables | A tiles (one 16 KB 128 x 64 BF16
+// tile per decoder group, 1024-aligned) | x ring (nx slots of bn*128 bytes)
+// | compressed slots (two per group) | pad. The x ring gets ndg slots when
+// they fit (then an x slot is freed by the same commit as its group's A
+// tile), else as many as fit.
 GemmLayout gemm_layout(int ndg, int bn, uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r,
                        int smem_limit) {
     GemmLayout l{};
-    l.off_rb = kBarrierBytes + kTableBytes;
-    l.off_x = round_up(l.off_rb + uint32_t(128 * ndg) * kRowBufferBytes, 1024);
+    l.off_a = round_up(kBarrierBytes + kTableBytes, 1024);
+    l.off_x = l.off_a + uint32_t(ndg) * kATileBytes;
     l.x_bytes = uint32_t(bn) * 128;
     l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r);
     const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
     const uint32_t used = l.off_x + slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    // More than two rounds of x slots (2 * ndg) buys nothing: the MMAs
-    // trail the decoders by less than that. At exactly 2 * ndg an x slot is
-    // freed by the same commit as the A buffer of its slice.
-    l.nx = std::min<int>({kMaxX, 2 * ndg, int(avail / l.x_bytes)});
+    l.nx = std::min<int>({kMaxX, ndg, int(avail / l.x_bytes)});
     l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
     l.total = l.off_slots + slots + kRingPadBytes;
     return l;
@@ -656,13 +660,12 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
             return cudaErrorInvalidValue;
         }
     }
-    // Four decoder groups when the x ring still gets three slots (the MMA
-    // runs two slices ahead of the x loads), else two.
+    // Four decoder groups when the x ring still gets two slots, else two.
     int ndg = 0;
     GemmLayout l{};
     for (int cand : {4, 2}) {
         l = gemm_layout(cand, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
-        if (l.nx >= 3 || (cand == 2 && l.nx >= 2)) {
+        if (l.nx >= 2) {
             ndg = cand;
             break;
         }
@@ -671,17 +674,16 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
         zs_set_error("zipgemm: packed payload capacity leaves no room for the shared-memory rings");
         return cudaErrorInvalidConfiguration;
     }
-    // Split-K reduction reuses the rings: they must hold a bn x 128 FP32 tile.
-    if (kparts > 1 && uint32_t(p.bn) * 128 * 4 > l.total - kRingPadBytes - l.off_x)
+    // Split-K reduction reuses the A tiles and rings: they must hold a
+    // bn x 128 FP32 tile.
+    if (kparts > 1 && uint32_t(p.bn) * 128 * 4 > l.total - kRingPadBytes - l.off_a)
         kparts = p.kparts = 1;
     p.nx = l.nx;
-    p.off_rb = l.off_rb, p.off_x = l.off_x;
+    p.off_a = l.off_a, p.off_x = l.off_x;
     p.off_slots = l.off_slots, p.x_bytes = l.x_bytes, p.slot = l.slot;
-    p.a_col0 = uint32_t(std::max(p.bn, 32));
-    // Two A buffers per group when they fit in the A-buffer barriers and TMEM.
-    // Two TMEM A buffers per decoder group (a_col0 + 64 * ndg <= 512 columns).
+    // TMEM holds only the FP32 accumulator (bn columns).
     uint32_t cols = 32;
-    while (cols < p.a_col0 + 64u * uint32_t(ndg)) cols <<= 1;
+    while (cols < uint32_t(p.bn)) cols <<= 1;
     p.tmem_cols = cols;
 
     // x viewed as [K/64][N][64]: one box = one K slice of bn tokens, a

@@ -9,10 +9,11 @@ namespace zs {
 
 constexpr int kMaxStages = 8;    // compressed ring slots
 constexpr int kMaxX = 8;         // x ring slots (one K slice each)
-constexpr int kMaxABuffers = 8;  // TMEM A buffers (32 columns each)
+constexpr int kMaxGroups = 4;    // decoder groups (one A tile each)
 constexpr int kBarrierBytes = 1024;
 constexpr int kChunk = 32;       // K slices per refill of the offset / band-offset caches
 constexpr int kMaxGroup = 8;     // tiles per half of a compressed ring slot
+constexpr uint32_t kATileBytes = 128 * 128;  // decoded A tile: 128 rows x 64 BF16
 
 // A compressed ring slot holds two runs ("halves") of up to kMaxGroup tiles
 // that are consecutive in the packed streams (the fused GEMM: two tile rows
@@ -45,10 +46,10 @@ struct GemmParams {
     uint32_t cap_c, cap_r;  // payload capacity per tile (bytes, words)
     uint32_t start_exp;
     uint32_t plane_box_bytes;  // bytes one bitmap tensor load (or three) writes
-    uint32_t off_rb, off_x, off_slots;
+    uint32_t off_a, off_x, off_slots;
     uint32_t x_bytes;      // one x slot: bn tokens x one K slice (bn * 128 bytes)
     SlotLayout slot;       // one K slice of the block's two tile rows
-    uint32_t a_col0, tmem_cols;
+    uint32_t tmem_cols;
 };
 
 struct DecompressParams {
@@ -63,7 +64,7 @@ struct DecompressParams {
     int plane_maps;
     uint32_t cap_c, cap_r;
     uint32_t start_exp;
-    uint32_t off_rb, off_out, off_slots;
+    uint32_t off_out, off_slots;
     SlotLayout slot;
 };
 
