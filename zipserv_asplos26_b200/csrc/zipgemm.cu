@@ -50,8 +50,7 @@
 
 namespace zs {
 
-constexpr int kGemmThreads4 = 128 + 128 * 4;
-constexpr int kGemmThreads2 = 128 + 128 * 2;
+constexpr int gemm_threads(int ndg) { return 128 + 128 * ndg; }
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
 __host__ __device__ __forceinline__ int lane_row(int slot) {
@@ -81,8 +80,8 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
     const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
     const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
     const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [NDG] group's A tile written
-    const uint32_t bar_aempty = bar_afull + 8 * kMaxGroups;   // [NDG] A tile read by the MMAs
-    const uint32_t bar_xfull = bar_aempty + 8 * kMaxGroups;   // [kMaxX]
+    const uint32_t bar_aempty = bar_afull + 8 * kMaxATiles;  // [abuf*NDG] A tile read by MMAs
+    const uint32_t bar_xfull = bar_aempty + 8 * kMaxATiles;   // [kMaxX]
     const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
     const uint32_t bar_d = bar_xempty + 8 * kMaxX;
     const uint32_t bar_tab = bar_d + 8;
@@ -108,7 +107,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             ptx::mbar_init(bar_addr(bar_xfull, i), 1);
             ptx::mbar_init(bar_addr(bar_xempty, i), 1);
         }
-        for (int i = 0; i < NDG; ++i) {
+        for (int i = 0; i < 2 * NDG; ++i) {
             ptx::mbar_init(bar_addr(bar_afull, i), 4);   // the group's four warps
             ptx::mbar_init(bar_addr(bar_aempty, i), 1);  // MMA commit
         }
@@ -136,7 +135,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
     if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
         // Slice k = NDG*u + g: A = group g's shared-memory tile (use u),
-        // B = x slot k % nx. With nx == NDG the x slot is the group's index
+        // B = x slot k % nx. With nx == abuf * NDG the x slot is the A tile's index
         // and one commit frees both. Indices are kept as counters: this
         // thread shares its sub-partition with decoder warps.
         if (lane == 0) {
@@ -144,28 +143,31 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
             const uint32_t abase = sbase + p.off_a;
             const int nx = p.nx;
-            const bool xmerged = nx == NDG;
+            const int ashift = p.abuf - 1;  // A tiles per group: 1 or 2
+            const bool xmerged = nx == p.abuf * NDG;
             int xs = 0;
             uint32_t xph = 0;
             bool ok = true;
             for (int u = 0, k = 0; ok && k < nk; ++u) {
-                const uint32_t aph = uint32_t(u) & 1u;
+                const uint32_t aph = uint32_t(u >> ashift) & 1u;
+                const int aoff = (u & ashift) * NDG;
 #pragma unroll
                 for (int g = 0; g < NDG; ++g) {
                     if (k >= nk) break;
                     if (!ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) ||
-                        !ptx::mbar_wait(bar_addr(bar_afull, g), aph)) {
+                        !ptx::mbar_wait(bar_addr(bar_afull, g + aoff), aph)) {
                         ok = false;
                         break;
                     }
                     ptx::tc_fence_after();
                     const uint64_t bdesc = ptx::smem_desc_sw128(xbase + uint32_t(xs) * xstep);
-                    const uint64_t adesc = ptx::smem_desc_sw128(abase + uint32_t(g) * kATileBytes);
+                    const uint64_t adesc =
+                        ptx::smem_desc_sw128(abase + uint32_t(g + aoff) * kATileBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         ptx::mma_bf16_ss(tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
                                          (k | kk) != 0);
-                    ptx::mma_commit(bar_addr(bar_aempty, g));
+                    ptx::mma_commit(bar_addr(bar_aempty, g + aoff));
                     if (!xmerged) ptx::mma_commit(bar_addr(bar_xempty, xs));
                     if (++xs == nx) xs = 0, xph ^= 1u;
                     ++k;
@@ -184,7 +186,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             int issued = 0;
             for (int k = 0; k < nk; ++k) {
                 const int xs = k % nx;
-                const uint32_t freed = nx == NDG ? bar_aempty : bar_xempty;
+                const uint32_t freed = nx == p.abuf * NDG ? bar_aempty : bar_xempty;
                 if (k >= nx && !ptx::mbar_wait(bar_addr(freed, xs), ((k / nx) - 1) & 1)) break;
                 ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
                 ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0,
@@ -285,7 +287,7 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
         // This thread's row of the group's A tile: MMA row m = 32*q + lane
         // (= accumulator lane), 128-byte swizzled.
         const uint32_t m = uint32_t(32 * q + lane);
-        const uint32_t arow = sbase + p.off_a + uint32_t(g) * kATileBytes + (m >> 3) * 1024u +
+        const uint32_t arow = sbase + p.off_a + (m >> 3) * 1024u +
                               (m & 7u) * 128u;
         const uint32_t swz = (m & 7u) << 4;
         const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
@@ -306,15 +308,18 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             }
             // The A tile is free once the MMAs of the group's previous slice
             // finished reading it.
-            if (u > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, g), (u - 1) & 1);
+            // A tile a = g + NDG * (u % abuf), use u / abuf.
+            const int ashift = p.abuf - 1;
+            const int a = g + (u & ashift) * NDG, ause = u >> ashift;
+            if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
-            dec.store(arow, swz, out, rs, slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
+            dec.store(arow + uint32_t(a) * kATileBytes, swz, out, rs, slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
             // Generic-proxy stores must be visible to the tensor cores.
             ptx::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
                 ptx::mbar_arrive(bar_addr(bar_free, sidx));  // slot fully read
-                ptx::mbar_arrive(bar_addr(bar_afull, g));
+                ptx::mbar_arrive(bar_addr(bar_afull, a));
             }
         }
     }
@@ -437,22 +442,22 @@ struct GemmLayout {
     int nx;
 };
 
-// Shared memory: barriers | lookup tables | A tiles (one 16 KB 128 x 64 BF16
-// tile per decoder group, 1024-aligned) | x ring (nx slots of bn*128 bytes)
-// | compressed slots (two per group) | pad. The x ring gets ndg slots when
-// they fit (then an x slot is freed by the same commit as its group's A
-// tile), else as many as fit.
-GemmLayout gemm_layout(int ndg, int bn, uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r,
-                       int smem_limit) {
+// Shared memory: barriers | lookup tables | A tiles (abuf 16 KB 128 x 64
+// BF16 tiles per decoder group, 1024-aligned) | x ring (nx slots of bn*128
+// bytes) | compressed slots (two per group) | pad. The x ring gets one slot
+// per A tile when they fit (then an x slot is freed by the same commit as
+// its A tile), else as many as fit.
+GemmLayout gemm_layout(int ndg, int abuf, int bn, uint32_t plane_pitch, uint32_t cap_c,
+                       uint32_t cap_r, int smem_limit) {
     GemmLayout l{};
     l.off_a = round_up(kBarrierBytes + kTableBytes, 1024);
-    l.off_x = l.off_a + uint32_t(ndg) * kATileBytes;
+    l.off_x = l.off_a + uint32_t(ndg * abuf) * kATileBytes;
     l.x_bytes = uint32_t(bn) * 128;
     l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r);
     const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
     const uint32_t used = l.off_x + slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    l.nx = std::min<int>({kMaxX, ndg, int(avail / l.x_bytes)});
+    l.nx = std::min<int>({kMaxX, ndg * abuf, int(avail / l.x_bytes)});
     l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
     l.total = l.off_slots + slots + kRingPadBytes;
     return l;
@@ -548,7 +553,7 @@ static int active_clusters(int device, int size, uint32_t smem) {
     if (d.active_clusters[size]) return d.active_clusters[size];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(size * 64, 1, 1);
-    cfg.blockDim = dim3(kGemmThreads4, 1, 1);
+    cfg.blockDim = dim3(gemm_threads(4), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -571,7 +576,7 @@ static cudaError_t ensure_gemm_attributes(int device) {
     DeviceInfo& d = device_info(device);
     if (d.gemm_attr) return cudaSuccess;
     cudaError_t e = cudaSuccess;
-    for (auto fn : {zipgemm_kernel<4>, zipgemm_kernel<2>}) {
+    for (auto fn : {zipgemm_kernel<4>, zipgemm_kernel<3>, zipgemm_kernel<2>}) {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      d.smem_optin);
@@ -660,13 +665,21 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
             return cudaErrorInvalidValue;
         }
     }
-    // Four decoder groups when the x ring still gets two slots, else two.
+    // (decoder groups, A tiles per group), best first (measured): four
+    // groups with one A tile each (more decode throughput, some stalls on
+    // the previous slice's MMAs), then fewer groups with double-buffered A
+    // tiles. The x ring needs at least two slots.
+    struct Choice {
+        int ndg, abuf;
+    };
+    constexpr Choice kChoices[] = {{4, 1}, {3, 2}, {2, 2}, {2, 1}};
     int ndg = 0;
     GemmLayout l{};
-    for (int cand : {4, 2}) {
-        l = gemm_layout(cand, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
+    for (const Choice& c : kChoices) {
+        l = gemm_layout(c.ndg, c.abuf, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
         if (l.nx >= 2) {
-            ndg = cand;
+            ndg = c.ndg;
+            p.abuf = c.abuf;
             break;
         }
     }
@@ -700,7 +713,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(((m / 64 + 1) / 2) * kparts), unsigned((n + p.bn - 1) / p.bn), 1);
-    cfg.blockDim = dim3(ndg == 4 ? kGemmThreads4 : kGemmThreads2, 1, 1);
+    cfg.blockDim = dim3(gemm_threads(ndg), 1, 1);
     cfg.dynamicSmemBytes = l.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -710,8 +723,9 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = ndg == 4 ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<4>, xmap, pm, mmap, p)
-                 : cudaLaunchKernelEx(&cfg, zipgemm_kernel<2>, xmap, pm, mmap, p);
+    e = ndg == 4   ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<4>, xmap, pm, mmap, p)
+        : ndg == 3 ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<3>, xmap, pm, mmap, p)
+                   : cudaLaunchKernelEx(&cfg, zipgemm_kernel<2>, xmap, pm, mmap, p);
     if (e != cudaSuccess) {
         char msg[220];
         snprintf(msg, sizeof(msg),

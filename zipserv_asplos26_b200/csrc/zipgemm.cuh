@@ -9,7 +9,7 @@ namespace zs {
 
 constexpr int kMaxStages = 8;    // compressed ring slots
 constexpr int kMaxX = 8;         // x ring slots (one K slice each)
-constexpr int kMaxGroups = 4;    // decoder groups (one A tile each)
+constexpr int kMaxATiles = 8;    // decoded A tiles (decoder groups x tiles per group)
 constexpr int kBarrierBytes = 1024;
 constexpr int kChunk = 32;       // K slices per refill of the offset / band-offset caches
 constexpr int kMaxGroup = 8;     // tiles per half of a compressed ring slot
@@ -43,6 +43,7 @@ struct GemmParams {
     int kparts;            // CTAs per cluster along K
     int bn;                // N tile (multiple of 16, <= 256)
     int nx;                // x ring slots
+    int abuf;              // decoded A tiles per decoder group (1 or 2)
     uint32_t cap_c, cap_r;  // payload capacity per tile (bytes, words)
     uint32_t start_exp;
     uint32_t plane_box_bytes;  // bytes one bitmap tensor load (or three) writes
