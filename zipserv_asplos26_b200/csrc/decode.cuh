@@ -79,8 +79,7 @@ struct RareState {
 
 struct RowDecoder {
     uint32_t ct;         // shared address of code table + lane*4
-    uint32_t selr;       // byte-permute selector: byte (r & 3) of a, zeros elsewhere
-    int bm_word;         // u32 index of this row's bitmap word inside one plane
+    uint32_t bm_byte;    // offset of this row's bitmap byte (segment 0) inside one plane
     int band;            // 16-row band inside the tile
     uint32_t lane16;     // lane inside the 16-lane half
     uint32_t row_elems;  // 64*rt + 8*r: elements before this row in its small-tile pair
@@ -98,8 +97,8 @@ struct RowDecoder {
         const int r = lane & 7, rt = (lane >> 3) & 1;
         band = band_;
         ct = tables_smem + uint32_t(lane) * 4u;
-        selr = uint32_t(r & 3) | 0x4440u;
-        bm_word = (band * 16 + rt) * 2 + (r >> 2);
+        // Small tile (band, j, rt) is bitmap word pair band*16 + 2j + rt; byte r is row r.
+        bm_byte = uint32_t((band * 16 + rt) * 8 + r);
         lane16 = uint32_t(lane) & 15u;
         row_elems = uint32_t(64 * rt + 8 * r);
         uint32_t xp[2] = {0, 0};
@@ -128,15 +127,15 @@ struct RowDecoder {
     __device__ __forceinline__ void decode(uint32_t plane, uint32_t plane_stride, uint32_t medium,
                                            uint32_t common, uint32_t cap_c, uint32_t cap_r,
                                            uint32_t (&out)[32], RareState& rs) const {
-        plane += uint32_t(bm_word) * 4u;
+        plane += bm_byte;
         const int2 med = ptx::lds_s64(medium + uint32_t(band) * 8u);
         uint32_t code[8], flag[8], ind[8];
         uint32_t k0 = 0, k1 = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const uint32_t m1 = __byte_perm(ptx::lds_s32(plane + 16u * j), 0, selr);
-            const uint32_t m2 = __byte_perm(ptx::lds_s32(plane + plane_stride + 16u * j), 0, selr);
-            const uint32_t m3 = __byte_perm(ptx::lds_s32(plane + 2u * plane_stride + 16u * j), 0, selr);
+            const uint32_t m1 = ptx::lds_u8(plane + 16u * j);
+            const uint32_t m2 = ptx::lds_u8(plane + plane_stride + 16u * j);
+            const uint32_t m3 = ptx::lds_u8(plane + 2u * plane_stride + 16u * j);
             const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, k128, ct));
             const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, k128, ct));
             const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, k128, ct));
@@ -226,24 +225,27 @@ struct RowDecoder {
                         make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]));
         uint32_t rlo = all_common ? 0u : ~rs.i03, rhi = all_common ? 0u : ~rs.i47;
         const uint32_t rcap = cap_r ? cap_r - 1 : 0;
+        // Rares are visited in row order; `run` counts the rares already
+        // patched in the current segment, so the word of the rare at (j, c)
+        // is ro_j + run.
+        uint32_t prev = 8u, run = 0u;
         while (rlo | rhi) {
-            uint32_t p;
-            if (rlo) {
-                p = __ffs(rlo) - 1;
-                rlo &= rlo - 1;
-            } else {
-                p = 31 + __ffs(rhi);
-                rhi &= rhi - 1;
-            }
-            const uint32_t j = p >> 3, c = p & 7;
-            const uint32_t seg_ind = __byte_perm(rs.i03, rs.i47, j);  // byte j
-            const uint32_t pair = (j >> 1) < 2
-                                      ? __byte_perm(rs.ro[0], rs.ro[1], (j & 2) ? 0x7654 : 0x3210)
-                                      : __byte_perm(rs.ro[2], rs.ro[3], (j & 2) ? 0x7654 : 0x3210);
-            const uint32_t base = (j & 1) ? (pair >> 16) : (pair & 0xFFFFu);
-            const uint32_t idx = base + c - __popc(seg_ind & 0xFFu & ((1u << c) - 1u));
-            const uint32_t word = ptx::lds_u16(rare + 2u * min(idx & 0xFFFFu, rcap));
-            ptx::sts16(row + (((j << 4) ^ swz) | (c << 1)), word);
+            const bool hi = rlo == 0u;
+            const uint32_t m = hi ? rhi : rlo;
+            const uint32_t p = uint32_t(__ffs(m) - 1) + (hi ? 32u : 0u);  // 0..63
+            const uint32_t m2 = m & (m - 1u);
+            rlo = hi ? rlo : m2;
+            rhi = hi ? m2 : rhi;
+            const uint32_t j = p >> 3;
+            run = j == prev ? run + 1u : 0u;
+            prev = j;
+            // ro_j: 16-bit lane (j & 3) of the pair of words holding segments 4*hi .. 4*hi+3.
+            const uint32_t ro = __byte_perm(hi ? rs.ro[2] : rs.ro[0], hi ? rs.ro[3] : rs.ro[1],
+                                            (j & 3u) * 0x22u + 0x10u);
+            const uint32_t idx = min((ro + run) & 0xFFFFu, rcap);
+            const uint32_t word = ptx::lds_u16(rare + 2u * idx);
+            // Element c of segment j: byte 2c of 16-byte chunk j, swizzled.
+            ptx::sts16(row + (((2u * p) & 0x7Eu) ^ swz), word);
         }
     }
 };

@@ -136,9 +136,10 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
         // ------------------------------------------------------ MMA issuer
         // Slice k = NDG*u + g: A = group g's shared-memory tile (use u),
         // B = x slot k % nx. With nx == abuf * NDG the x slot is the A tile's index
-        // and one commit frees both. Indices are kept as counters: this
-        // thread shares its sub-partition with decoder warps.
-        if (lane == 0) {
+        // and one commit frees both. The whole warp runs the loop in uniform
+        // control flow (descriptors in uniform registers); one elected lane
+        // issues each MMA and commit.
+        {
             const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
             const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
             const uint32_t abase = sbase + p.off_a;
@@ -154,8 +155,9 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 #pragma unroll
                 for (int g = 0; g < NDG; ++g) {
                     if (k >= nk) break;
-                    if (!ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) ||
-                        !ptx::mbar_wait(bar_addr(bar_afull, g + aoff), aph)) {
+                    ok = ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) &&
+                         ptx::mbar_wait(bar_addr(bar_afull, g + aoff), aph);
+                    if (!__all_sync(kFullMask, ok)) {
                         ok = false;
                         break;
                     }
@@ -165,15 +167,15 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
                         ptx::smem_desc_sw128(abase + uint32_t(g + aoff) * kATileBytes);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        ptx::mma_bf16_ss(tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
-                                         (k | kk) != 0);
-                    ptx::mma_commit(bar_addr(bar_aempty, g + aoff));
-                    if (!xmerged) ptx::mma_commit(bar_addr(bar_xempty, xs));
+                        ptx::mma_bf16_ss_elect(tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                               (k | kk) != 0);
+                    ptx::mma_commit_elect(bar_addr(bar_aempty, g + aoff));
+                    if (!xmerged) ptx::mma_commit_elect(bar_addr(bar_xempty, xs));
                     if (++xs == nx) xs = 0, xph ^= 1u;
                     ++k;
                 }
             }
-            ptx::mma_commit(bar_d);  // fires once every issued MMA has finished
+            ptx::mma_commit_elect(bar_d);  // fires once every issued MMA has finished
         }
         __syncwarp();
     } else if (warp == 4 * NDG + 1) {
