@@ -12,8 +12,13 @@
  * Conventions shared by the GPU entry points:
  *   - All device buffers belong to the caller and must stay alive until the
  *     enqueued work completes. Work is enqueued on `stream` (a cudaStream_t,
- *     NULL = legacy default stream); no host synchronisation, no device
- *     allocation, so calls can be captured in CUDA graphs.
+ *     NULL = legacy default stream) without host synchronisation, so calls
+ *     can be captured in CUDA graphs. The only device allocation is the
+ *     GEMM's K-range scratch: zipserv_mm, zipserv_mm_fp32 and
+ *     zipserv_mm_kparts keep one library-owned buffer per (device, stream),
+ *     allocated on the first launch that needs it and grown on demand, never
+ *     while the stream is being captured (run a shape once before capturing
+ *     it); zipserv_mm_ws takes the scratch from the caller instead.
  *   - Return 0 (cudaSuccess) or a cudaError_t value; on failure
  *     zipserv_error() describes it. Contract violations, including null
  *     pointers and device buffers not aligned to 16 bytes, return
@@ -83,14 +88,36 @@ int zipserv_mm_fp32(void* stream, const void* sm, const void* rare, const void* 
 
 /* ---- Extensions (no counterpart in the reference bridge) ---------------- */
 
-/* zipserv_mm with an explicit in-kernel K partition: the K tiles are split
- * over `k_parts` CTAs of one thread-block cluster (1..16, at most k/64) whose
- * FP32 partial sums are reduced through distributed shared memory.
- * k_parts = 0 picks the partition for the device, as zipserv_mm does. */
+/* zipserv_mm with an explicit K partition: k_parts CTAs per 128-row block
+ * (1..16, at most k/64) instead of the default persistent grid of one CTA
+ * per SM. Rows whose K range is split over CTAs are summed in FP32, in K
+ * order (deterministic), by the last CTA to finish them.
+ * k_parts = 0 is the default schedule, as zipserv_mm uses. */
 int zipserv_mm_kparts(void* stream, const void* sm, const void* rare, const void* b1,
                       const void* b2, const void* b3, const void* medium, const void* global,
                       int max_common, int max_rare, int start_exp, const void* x, void* y,
                       int m, int n, int k, int k_parts);
+
+/* Scratch zipserv_mm_ws needs for this shape and k_parts (as in
+ * zipserv_mm_kparts) on the current device: *partial_bytes for FP32 partial
+ * tiles and *counter_bytes for arrival counters; both 0 when no CTA's K
+ * range splits a row block. Returns 0, or cudaErrorInvalidValue (both sizes
+ * 0) for an invalid shape or k_parts. */
+int zipserv_mm_workspace_size(int m, int n, int k, int k_parts, uint64_t* partial_bytes,
+                              uint64_t* counter_bytes);
+
+/* zipserv_mm_kparts with caller-owned scratch; allocates nothing. Both
+ * buffers 16-byte aligned and at least the sizes zipserv_mm_workspace_size
+ * reports. `partials` may hold anything. `counters` must be zero-filled
+ * before its first use; every launch returns the counters it used to zero,
+ * so one pair of buffers (sized for the largest shape) serves any sequence
+ * of launches, as long as no two of them run at the same time. Both may be
+ * null when the sizes are 0. */
+int zipserv_mm_ws(void* stream, const void* sm, const void* rare, const void* b1,
+                  const void* b2, const void* b3, const void* medium, const void* global,
+                  int max_common, int max_rare, int start_exp, const void* x, void* y, int m,
+                  int n, int k, int k_parts, void* partials, uint64_t partial_bytes,
+                  void* counters, uint64_t counter_bytes);
 
 /* The K partition zipserv_mm picks for this shape on the current device, or
  * a negative value if the shape is invalid. */

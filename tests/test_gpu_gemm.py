@@ -232,3 +232,50 @@ def test_unequally_spaced_bitmaps(native_lib, oracle_mod, m, k):
     torch.cuda.synchronize()
     assert np.array_equal(words_of(dense), w)
     assert runtime.device_flags() == 0
+
+
+@pytest.mark.parametrize("m,k,n,kparts", [(640, 1024, 40, 3), (256, 1024, 600, 5),
+                                          (192, 4096, 16, 0), (64, 64, 1, 0)])
+def test_split_rows_exact(native_lib, oracle_mod, m, k, n, kparts):
+    """Uneven CTA ranges: CTAs whose first and last row blocks are both split,
+    several N tiles, row blocks with one tile row; integer operands, exact."""
+    rng = oracle_mod.MT19937(m + k + n)
+    w = oracle_mod.integer_matrix(rng, m * k).reshape(m, k)
+    x = oracle_mod.integer_matrix(rng, n * k).reshape(n, k)
+    packed = runtime.compress(bf16_tensor(w)).to("cuda")
+    expected, _ = oracle_mod.gemm(w, x)
+    y = runtime.linear_kparts(bf16_tensor(x).cuda(), packed, kparts)
+    torch.cuda.synchronize()
+    assert np.array_equal(words_of(y), expected)
+    assert runtime.device_flags() == 0
+
+
+def test_caller_workspace(native_lib, oracle_mod):
+    """zipserv_mm_ws: caller scratch gives the library path's exact words,
+    one pair of buffers serves launches of different shapes in any order (the
+    counters return to zero), and undersized scratch is rejected."""
+    k = 2048
+    shapes = [(512, 24, 0), (512, 24, 3), (256, 300, 5), (512, 24, 16), (1024, 7, 0)]
+    sizes = [runtime.workspace_size(m, n, k, kp) for m, n, kp in shapes]
+    assert all(p > 0 and c > 0 for p, c in sizes)  # every shape here splits row blocks
+    partials = torch.full((max(p for p, _ in sizes),), 0x5A, dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(max(c for _, c in sizes), dtype=torch.uint8, device="cuda")
+    weights = {}
+    for rep in range(2):
+        for m, n, kp in (shapes if rep == 0 else shapes[::-1]):
+            if m not in weights:
+                w = oracle_mod.llama_weight(m, k, seed=7, outliers=0.02)
+                weights[m] = runtime.compress(bf16_tensor(w)).to("cuda")
+            packed = weights[m]
+            x = torch.randn(n, k, generator=torch.Generator().manual_seed(n)).to(torch.bfloat16).cuda()
+            ref = runtime.linear_kparts(x, packed, kp)
+            got = runtime.linear_kparts(x, packed, kp, workspace=(partials, counters))
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), (m, n, kp)
+            assert int(counters.count_nonzero()) == 0
+    p, c = sizes[0]
+    with pytest.raises(RuntimeError):
+        runtime.linear_kparts(x, weights[512], 0, workspace=(partials[: p - 16], counters))
+    # One CTA per row block splits nothing and needs no scratch.
+    assert runtime.workspace_size(256, 16, 256, 1) == (0, 0)
+    assert runtime.device_flags() == 0

@@ -29,7 +29,8 @@ cudaError_t fail(cudaError_t e, const char* what) {
 cudaError_t mm_impl(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
                     const void* b2, const void* b3, const void* medium, const void* global,
                     int max_common, int max_rare, int start_exp, const void* x, void* y, int m,
-                    int n, int k, const void* workspace, int split_k, int kparts) {
+                    int n, int k, const void* workspace, int split_k, int kparts,
+                    const zs::GemmScratch* scratch = nullptr) {
     if (!zs::valid_gemm(m, n, k, split_k) || !zs::valid_counts(max_common, max_rare))
         return fail(cudaErrorInvalidValue,
                     "invalid GEMM shape, Split-K or packed maxima (M, K multiples of 64; "
@@ -43,7 +44,7 @@ cudaError_t mm_impl(cudaStream_t stream, const void* sm, const void* rare, const
         (rare && !aligned16(rare)))
         return fail(cudaErrorInvalidValue, "device buffers must be 16-byte aligned");
     return zs::launch_zipgemm(stream, sm, rare, b1, b2, b3, medium, global, max_common,
-                              max_rare, start_exp, x, y, m, n, k, kparts);
+                              max_rare, start_exp, x, y, m, n, k, kparts, scratch);
 }
 
 cudaError_t decode_impl(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
@@ -147,6 +148,41 @@ extern "C" int zipserv_mm_kparts(void* stream, const void* sm, const void* rare,
     return int(mm_impl(static_cast<cudaStream_t>(stream), sm, rare, b1, b2, b3, medium, global,
                        max_common, max_rare, start_exp & 255, x, y, m, n, k, nullptr, 1,
                        k_parts));
+}
+
+extern "C" int zipserv_mm_workspace_size(int m, int n, int k, int k_parts,
+                                         uint64_t* partial_bytes, uint64_t* counter_bytes) {
+    if (!partial_bytes || !counter_bytes) return int(cudaErrorInvalidValue);
+    *partial_bytes = *counter_bytes = 0;
+    if (!zs::valid_gemm(m, n, k, 1) || k_parts < 0 || k_parts > 16 || k_parts > k / 64) {
+        zs_set_error("invalid GEMM shape or k_parts");
+        return int(cudaErrorInvalidValue);
+    }
+    if (n == 0) return 0;
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return int(e);
+    size_t p = 0, c = 0;
+    zs::gemm_workspace_bytes(m, n, k, k_parts, device, &p, &c);
+    *partial_bytes = p, *counter_bytes = c;
+    return 0;
+}
+
+extern "C" int zipserv_mm_ws(void* stream, const void* sm, const void* rare, const void* b1,
+                             const void* b2, const void* b3, const void* medium,
+                             const void* global, int max_common, int max_rare, int start_exp,
+                             const void* x, void* y, int m, int n, int k, int k_parts,
+                             void* partials, uint64_t partial_bytes, void* counters,
+                             uint64_t counter_bytes) {
+    if (k_parts < 0 || k_parts > 16 || (zs::valid_matrix(m, k) && k_parts > k / 64)) {
+        zs_set_error("k_parts must be in [0, min(16, K/64)]");
+        return int(cudaErrorInvalidValue);
+    }
+    const zs::GemmScratch scratch{partials, size_t(partial_bytes), counters,
+                                  size_t(counter_bytes)};
+    return int(mm_impl(static_cast<cudaStream_t>(stream), sm, rare, b1, b2, b3, medium, global,
+                       max_common, max_rare, start_exp & 255, x, y, m, n, k, nullptr, 1,
+                       k_parts, &scratch));
 }
 
 extern "C" int zipserv_mm_plan(int m, int n, int k) {

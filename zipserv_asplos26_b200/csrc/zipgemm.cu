@@ -2,13 +2,13 @@
 //
 //   y[n, m] = sum_k W[m, k] * x[n, k],  W decoded on the fly from TCA-TBE.
 //
-// One CTA computes a 128-row block of W (two vertically adjacent 64x64 global
-// tiles) against a tile of up to 256 tokens over a contiguous range of 64-wide
-// K slices. Warp roles (1 CTA per SM):
-//   warp 0      allocates tensor memory; lane 0 issues tcgen05.mma with
-//               both operands in shared memory (A = a decoder group's tile
-//               of decoded W, B = an x tile, both 128-byte swizzled) and the
-//               FP32 accumulator in TMEM;
+// A CTA computes 128-row blocks of W (two vertically adjacent 64x64 global
+// tiles) against a tile of up to 256 tokens over its range of 64-wide K
+// slices. Warp roles (1 CTA per SM):
+//   warp 0      allocates tensor memory and issues tcgen05.mma (one
+//               elected lane) with both operands in shared memory (A = a
+//               decoder group's tile of decoded W, B = an x tile, both
+//               128-byte swizzled) and two FP32 accumulators in TMEM;
 //   warps 1..   NDG decoder groups of four warps. Group g decodes K slices
 //               g, g+NDG, ... from two compressed slots it owns: while it
 //               decodes one, the other is filling. Warp w decodes 16-row
@@ -16,19 +16,21 @@
 //               row = 32*band + 16*tile + i); each thread rebuilds one W row
 //               (64 BF16) per slice in registers, writes it into the group's
 //               A tile with eight 16-byte stores and patches its rare
-//               elements with 16-bit stores;
+//               elements with 16-bit stores; the groups also drain the
+//               accumulators (epilogue);
 //   next warp   keeps an x ring of nx slices filled with 3-D TMA loads;
 //   last two    producers: fill the groups' slots as soon as a group releases
 //               one, with few, large copies (an SM's copy engine takes ~100
 //               cycles per copy whatever its size): one 4-D tensor load for
 //               the three bitmap planes of both tile rows, one 3-D load for
 //               the band offsets, one bulk copy per payload run.
-// Split-K: the CTAs of a thread-block cluster (1..16) share one row block and
-// split its K slices. Each writes its FP32 accumulator tile to its own shared
-// memory; after a cluster barrier every CTA reduces a disjoint part of the
-// tile by reading all partners' tiles through distributed shared memory in
-// rank order (deterministic), converts to BF16 and stores. No global
-// workspace and no second kernel (replaces csrc/Reduction_Kernel.cuh:16-41).
+// Split-K: the grid is persistent (one CTA per SM) and every CTA takes an
+// equal contiguous range of the (row block, K slice) work items, so each
+// gets the same amount of decoding whatever the shape. A row block whose K
+// range is split over several CTAs is summed through an FP32 workspace by
+// the last CTA to finish a piece of it, in K order (deterministic). No CTA
+// waits for another and no second kernel runs (replaces
+// csrc/Reduction_Kernel.cuh:16-41).
 //
 // Reference kernel this replaces: csrc/L_Kernel.cuh:310-915 (mma.sync,
 // cp.async double buffering, per-column-warp redundant decode).
@@ -41,6 +43,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "capi_internal.h"
 #include "codec.h"
@@ -50,7 +53,10 @@
 
 namespace zs {
 
-constexpr int gemm_threads(int ndg) { return 128 + 128 * ndg; }
+// Warpgroups: 0 = MMA issuer, x loader, two producers; 1 .. NDG = decoder
+// groups; NDG + 1 = epilogue.
+constexpr int gemm_threads(int ndg) { return 256 + 128 * ndg; }
+
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
 __host__ __device__ __forceinline__ int lane_row(int slot) {
@@ -62,16 +68,32 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
     return base + 8u * uint32_t(index);
 }
 
-// Warp roles: warp 0 allocates TMEM and its lane 0 issues the MMAs; warps
-// 1 .. 4*NDG form NDG decoder groups; warp 4*NDG+1 keeps the x ring filled;
-// the last two warps fill the decoder groups' compressed slots. Group g decodes K slices
-// g, g + NDG, ... and owns two compressed slots: while it decodes slice u
-// from one, the other is being filled with its next slice. A group issues
-// its own copies after a group barrier (no dedicated producer warp), lane 0
-// of each of its four warps taking a share, so copy issue is spread over the
-// four SM sub-partitions.
+// Work schedule (persistent, "stream-K"): a unit is one 128-row block x one
+// N tile; its kt K slices are the work items, units in order, so the grid's
+// steps = units * kt items form one sequence. CTA c owns the contiguous items
+// [start(c), start(c+1)), start(c) = c * steps / grid: every CTA gets the
+// same number of K slices (+-1) whatever the shape. The run of a CTA's items
+// inside one unit is a segment. A segment that covers its whole unit stores
+// BF16 output directly; a partial segment writes its FP32 partial tile to the
+// workspace, and the CTA that delivers a piece's last partial (an arrival
+// counter per unit piece) sums that piece's partials in K order - a fixed
+// order, so results do not depend on timing - converts and stores it, and
+// resets the counter. No CTA ever waits for another.
+__device__ __forceinline__ int step_start(int c, const GemmParams& p) {
+    return int(int64_t(c) * p.steps / p.grid);
+}
+__device__ __forceinline__ int step_owner(int item, const GemmParams& p) {
+    return int((int64_t(item + 1) * p.grid - 1) / p.steps);
+}
+
+// Warp roles: warp 0 allocates TMEM and issues the MMAs; warp 1 keeps the x
+// ring filled; warps 2-3 fill the decoder groups' compressed slots; warps
+// 4 .. 4 + 4*NDG - 1 form NDG decoder groups (local step t, item
+// start(c) + t, is decoded by group t % NDG from its slot 2*group +
+// ((t / NDG) & 1)); the last four warps drain the accumulators (epilogue),
+// one TMEM lane quarter each.
 template <int NDG>
-__global__ void __launch_bounds__(128 + 128 * NDG, 1)
+__global__ void __launch_bounds__(256 + 128 * NDG, 1)
     zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ PlaneMaps pm,
                    const __grid_constant__ CUtensorMap mmap, const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -79,25 +101,29 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
     const uint32_t sbase = ptx::smem_addr(smem);
     const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
     const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
-    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [NDG] group's A tile written
+    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [abuf*NDG] A tile written
     const uint32_t bar_aempty = bar_afull + 8 * kMaxATiles;  // [abuf*NDG] A tile read by MMAs
     const uint32_t bar_xfull = bar_aempty + 8 * kMaxATiles;   // [kMaxX]
     const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
-    const uint32_t bar_d = bar_xempty + 8 * kMaxX;
-    const uint32_t bar_tab = bar_d + 8;
+    const uint32_t bar_d = bar_xempty + 8 * kMaxX;             // [2] accumulator complete
+    const uint32_t bar_tempty = bar_d + 16;                    // [2] accumulator drained
+    const uint32_t bar_tab = bar_tempty + 16;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_tab - sbase) + 8);
     const uint32_t tables = sbase + kBarrierBytes;
+    constexpr int kEpiWarp = 4 + 4 * NDG;
 
-    const int S = p.kparts;
-    const int rank = int(blockIdx.x) % S;  // == %cluster_ctarank: clusters span S consecutive x
-    const int mblk = int(blockIdx.x) / S, nblk = int(blockIdx.y);
-    const int kt0 = int(int64_t(p.kt) * rank / S), kt1 = int(int64_t(p.kt) * (rank + 1) / S);
-    const int nk = kt1 - kt0;
-    const int tr0 = 2 * mblk;
-    const bool has1 = tr0 + 1 < p.row_tiles;
+    const int cta = int(blockIdx.x);
+    const int kt = p.kt, rbs = p.row_blocks;
+    const int t_begin = step_start(cta, p), t_end = step_start(cta + 1, p);
+    const int nsteps = t_end - t_begin;
+    const int unit0 = t_begin / kt;
+    const int nseg = nsteps > 0 ? (t_end - 1) / kt - unit0 + 1 : 0;
     const uint32_t cap_c = p.cap_c, cap_r = p.cap_r;
     const SlotLayout L = p.slot;
 
+    // The next kernel in the stream may start launching now; it waits for
+    // this grid's completion before it reads anything this grid writes.
+    ptx::launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < 2 * NDG; ++s) {
             ptx::mbar_init(bar_addr(bar_full, s), 1);
@@ -107,16 +133,19 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             ptx::mbar_init(bar_addr(bar_xfull, i), 1);
             ptx::mbar_init(bar_addr(bar_xempty, i), 1);
         }
-        for (int i = 0; i < 2 * NDG; ++i) {
+        for (int i = 0; i < kMaxATiles; ++i) {
             ptx::mbar_init(bar_addr(bar_afull, i), 4);   // the group's four warps
             ptx::mbar_init(bar_addr(bar_aempty, i), 1);  // MMA commit
         }
-        ptx::mbar_init(bar_d, 1);
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(bar_addr(bar_d, b), 1);
+            ptx::mbar_init(bar_addr(bar_tempty, b), 4);  // the epilogue warps
+        }
         ptx::mbar_init(bar_tab, 1);
         ptx::fence_mbar_init();
     }
     if (warp == 0) {
-        ptx::tmem_alloc(ptx::smem_addr(tmem_slot), p.tmem_cols);
+        ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 2 * p.tmem_cols);
         ptx::tmem_relinquish();
     }
     ptx::tc_fence_before();
@@ -134,97 +163,123 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
-        // Slice k = NDG*u + g: A = group g's shared-memory tile (use u),
-        // B = x slot k % nx. With nx == abuf * NDG the x slot is the A tile's index
-        // and one commit frees both. The whole warp runs the loop in uniform
-        // control flow (descriptors in uniform registers); one elected lane
-        // issues each MMA and commit.
-        {
-            const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
-            const uint32_t xbase = sbase + p.off_x, xstep = p.x_bytes;
-            const uint32_t abase = sbase + p.off_a;
-            const int nx = p.nx;
-            const int ashift = p.abuf - 1;  // A tiles per group: 1 or 2
-            const bool xmerged = nx == p.abuf * NDG;
-            int xs = 0;
-            uint32_t xph = 0;
-            bool ok = true;
-            for (int u = 0, k = 0; ok && k < nk; ++u) {
-                const uint32_t aph = uint32_t(u >> ashift) & 1u;
-                const int aoff = (u & ashift) * NDG;
+        // Step t: A = group t % NDG's tile a = t % (abuf * NDG), B = x slot
+        // t % nx (with nx == abuf * NDG the same index: one commit frees
+        // both). Segment s accumulates into TMEM buffer s & 1; its first MMA
+        // overwrites, and it waits until the epilogue of segment s - 2 has
+        // drained that buffer. The whole warp runs the loop in uniform
+        // control flow; one elected lane issues each MMA and commit.
+        const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
+        const int nx = p.nx, na = p.abuf * NDG;
+        const bool xmerged = nx == na;
+        // Descriptors advance by whole tiles: the start-address field holds
+        // address >> 4, so a tile of B bytes is B >> 4 in the descriptor.
+        const uint64_t xdesc0 = ptx::smem_desc_sw128(sbase + p.off_x);
+        const uint64_t adesc0 = ptx::smem_desc_sw128(sbase + p.off_a);
+        const uint32_t xstep = p.x_bytes >> 4, astep = kATileBytes >> 4;
+        int xs = 0, a = 0, s = 0, k = t_begin - unit0 * kt;
+        uint32_t xph = 0, aph = 0;
+        bool ok = true;
+        for (int t = 0; ok && t < nsteps; ++t) {
+            const bool first = t == 0 || k == 0, last = t == nsteps - 1 || k == kt - 1;
+            if (first && s >= 2)
+                ok = ptx::mbar_wait(bar_addr(bar_tempty, s & 1), uint32_t((s >> 1) - 1) & 1u);
+            ok = ok && ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) &&
+                 ptx::mbar_wait(bar_addr(bar_afull, a), aph);
+            if (!__all_sync(kFullMask, ok)) break;
+            ptx::tc_fence_after();
+            const uint32_t d = tmem + uint32_t(s & 1) * p.tmem_cols;
+            const uint64_t bdesc = xdesc0 + uint32_t(xs) * xstep;
+            const uint64_t adesc = adesc0 + uint32_t(a) * astep;
 #pragma unroll
-                for (int g = 0; g < NDG; ++g) {
-                    if (k >= nk) break;
-                    ok = ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) &&
-                         ptx::mbar_wait(bar_addr(bar_afull, g + aoff), aph);
-                    if (!__all_sync(kFullMask, ok)) {
-                        ok = false;
-                        break;
-                    }
-                    ptx::tc_fence_after();
-                    const uint64_t bdesc = ptx::smem_desc_sw128(xbase + uint32_t(xs) * xstep);
-                    const uint64_t adesc =
-                        ptx::smem_desc_sw128(abase + uint32_t(g + aoff) * kATileBytes);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        ptx::mma_bf16_ss_elect(tmem, adesc + 2u * kk, bdesc + 2u * kk, idesc,
-                                               (k | kk) != 0);
-                    ptx::mma_commit_elect(bar_addr(bar_aempty, g + aoff));
-                    if (!xmerged) ptx::mma_commit_elect(bar_addr(bar_xempty, xs));
-                    if (++xs == nx) xs = 0, xph ^= 1u;
-                    ++k;
-                }
-            }
-            ptx::mma_commit_elect(bar_d);  // fires once every issued MMA has finished
+            for (int kk = 0; kk < 4; ++kk)
+                ptx::mma_bf16_ss_elect(d, adesc + 2u * kk, bdesc + 2u * kk, idesc,
+                                       !(first && kk == 0));
+            ptx::mma_commit_elect(bar_addr(bar_aempty, a));
+            if (!xmerged) ptx::mma_commit_elect(bar_addr(bar_xempty, xs));
+            if (last) ptx::mma_commit_elect(bar_addr(bar_d, s & 1));  // segment complete
+            if (++xs == nx) xs = 0, xph ^= 1u;
+            if (++a == na) a = 0, aph ^= 1u;
+            if (++k == kt) k = 0;
+            if (last) ++s;
         }
         __syncwarp();
-    } else if (warp == 4 * NDG + 1) {
+    } else if (warp == 1) {
         // ------------------------------------------------------ x loader
-        // Slice k's x tile goes to x slot k % nx once the MMAs of slice
-        // k - nx have finished reading that slot.
+        // Step t's x tile goes to x slot t % nx once the MMAs of step t - nx
+        // have finished reading that slot. x may be written by the previous
+        // kernel in the stream: wait for it first.
         if (lane == 0) {
+            ptx::wait_prerequisites();
             const uint64_t pol_x = ptx::policy_evict_last();
             const int nx = p.nx;
-            int issued = 0;
-            for (int k = 0; k < nk; ++k) {
-                const int xs = k % nx;
-                const uint32_t freed = nx == p.abuf * NDG ? bar_aempty : bar_xempty;
-                if (k >= nx && !ptx::mbar_wait(bar_addr(freed, xs), ((k / nx) - 1) & 1)) break;
+            const uint32_t freed = nx == p.abuf * NDG ? bar_aempty : bar_xempty;
+            int issued = 0, k = t_begin - unit0 * kt, xs = 0;
+            int ntok = (unit0 / rbs) * p.bn, rb = unit0 % rbs;  // token offset of the unit
+            uint32_t fph = 0;  // parity of the `freed` completion awaited next
+            for (int t = 0; t < nsteps; ++t) {
+                if (t >= nx && !ptx::mbar_wait(bar_addr(freed, xs), fph)) break;
                 ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
-                ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0,
-                                 nblk * p.bn, kt0 + k, bar_addr(bar_xfull, xs), pol_x);
-                issued = k + 1;
+                ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0, ntok, k,
+                                 bar_addr(bar_xfull, xs), pol_x);
+                issued = t + 1;
+                if (++xs == nx) {
+                    xs = 0;
+                    if (t >= nx) fph ^= 1u;
+                }
+                if (++k == kt) {
+                    k = 0;
+                    if (++rb == rbs) rb = 0, ntok += p.bn;
+                }
             }
             // Never leave copies in flight: wait for the last loads to land.
-            for (int k = max(0, issued - nx); k < issued; ++k)
-                ptx::mbar_wait(bar_addr(bar_xfull, k % nx), (k / nx) & 1);
+            for (int t = max(0, issued - nx); t < issued; ++t)
+                ptx::mbar_wait(bar_addr(bar_xfull, t % nx), (t / nx) & 1);
         }
         __syncwarp();
-    } else if (warp >= 4 * NDG + 2) {
+    } else if (warp < 4) {
         // ------------------------------------------------------ producers
-        // Producer pi fills the compressed slots of slices pi, pi + 2, ...
-        // (slice k goes to group k % NDG, slot 2 * group + ((k / NDG) & 1))
+        // Producer pi fills the compressed slots of steps pi, pi + 2, ...
+        // (step t goes to group t % NDG, slot 2 * group + ((t / NDG) & 1))
         // once the group has released the slot's previous contents. Per
         // slot: one 4-D tensor load for the three bitmap planes of both tile
         // rows, one 3-D load for the band offsets and one bulk copy per
-        // payload run, all completing on the slot's barrier.
-        const int pi = warp - (4 * NDG + 2);
+        // payload run, all completing on the slot's barrier. The packed
+        // weight is never written by other kernels: no prerequisite wait.
+        const int pi = warp - 2;
         const int2* goffs = reinterpret_cast<const int2*>(p.global);
         const uint64_t pol_w = ptx::policy_evict_first();
-        // Lanes 0-3 hold the (common, rare) offsets of slice k: lane 2*t + e
-        // = entry e (0 start, 1 end) of tile row t.
-        auto load_offsets = [&](int k) {
+        // Position (K slice, row block) of a step, advanced without divisions.
+        struct Pos {
+            int k, rb;
+        };
+        auto advance = [&](Pos& q, int steps) {
+            q.k += steps;
+            while (q.k >= kt) {
+                q.k -= kt;
+                if (++q.rb == rbs) q.rb = 0;
+            }
+        };
+        // Lanes 0-3 hold the (common, rare) offsets of a step: lane 2*r + e
+        // = entry e (0 start, 1 end) of tile row r of the step's block.
+        auto load_offsets = [&](int t, const Pos& q) {
             int2 v = make_int2(0, 0);
-            if (k < nk && lane < 4 && ((lane >> 1) == 0 || has1))
-                v = goffs[size_t(tr0 + (lane >> 1)) * p.kt + kt0 + k + (lane & 1)];
+            if (t < nsteps && lane < 4) {
+                const int tr = 2 * q.rb + (lane >> 1);
+                if (tr < p.row_tiles) v = goffs[size_t(tr) * kt + q.k + (lane & 1)];
+            }
             return v;
         };
-        int2 o = load_offsets(pi);
+        Pos cur{t_begin - unit0 * kt, unit0 % rbs};
+        advance(cur, pi);
+        Pos nxt = cur;
+        advance(nxt, 2);
+        int2 o = load_offsets(pi, cur);
         bool ok = true;
-        int last = -1;  // last slice issued
-        for (int k = pi; k < nk; k += 2) {
-            const int2 onext = load_offsets(k + 2);
-            const int g = k % NDG, u = k / NDG, sidx = g * 2 + (u & 1);
+        int last = -1;  // last step issued
+        for (int t = pi, u = pi / NDG, g = pi % NDG; t < nsteps; t += 2) {
+            const int2 onext = load_offsets(t + 2, nxt);
+            const int sidx = g * 2 + (u & 1);
             int2 e[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -232,23 +287,24 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
             if (lane == 0) {
                 if (u >= 2) ok = ptx::mbar_wait(bar_addr(bar_free, sidx), ((u >> 1) - 1) & 1);
                 if (ok) {
+                    const int kc = cur.k, tr0 = 2 * cur.rb;
+                    const bool has1 = tr0 + 1 < p.row_tiles;
                     uint32_t clen[2], rlen[2];
 #pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const int2 st = e[2 * t], en = e[2 * t + 1];
-                        const bool live = t == 0 || has1;
+                    for (int r = 0; r < 2; ++r) {
+                        const int2 st = e[2 * r], en = e[2 * r + 1];
+                        const bool live = r == 0 || has1;
                         // Payload copies need 16-byte aligned sources, which
                         // the offsets of valid packed data always give.
-                        clen[t] = live && (st.x & 15) == 0
+                        clen[r] = live && (st.x & 15) == 0
                                       ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
                                       : 0u;
-                        rlen[t] = live && (st.y & 7) == 0
+                        rlen[r] = live && (st.y & 7) == 0
                                       ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
                                       : 0u;
                     }
                     const uint32_t slot = sbase + p.off_slots + uint32_t(sidx) * L.bytes;
                     const uint32_t full = bar_addr(bar_full, sidx);
-                    const int kc = kt0 + k;
                     ptx::mbar_arrive_expect_tx(full, p.plane_box_bytes + 64u + clen[0] + clen[1] +
                                                          rlen[0] + rlen[1]);
                     if (pm.count == 1) {
@@ -264,43 +320,53 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
                     if (clen[1]) ptx::bulk_g2s(slot + L.common1, p.sm + e[2].x, clen[1], full, pol_w);
                     if (rlen[0]) ptx::bulk_g2s(slot + L.rare0, p.rare + e[0].y, rlen[0], full, pol_w);
                     if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[2].y, rlen[1], full, pol_w);
-                    last = k;
+                    last = t;
                 }
             }
             if (!__shfl_sync(kFullMask, ok, 0)) break;
             o = onext;
+            cur = nxt;
+            advance(nxt, 2);
+            if ((g += 2) >= NDG) g -= NDG, ++u;
         }
         // Never leave copies in flight: wait (bounded) for the last use of
         // every slot this producer filled.
         if (lane == 0)
-            for (int k = max(pi, last - 2 * NDG + 2); k >= 0 && k <= last; k += 2) {
-                const int g = k % NDG, u = k / NDG;
+            for (int t = max(pi, last - 2 * NDG + 2); t >= 0 && t <= last; t += 2) {
+                const int g = t % NDG, u = t / NDG;
                 ptx::mbar_wait(bar_addr(bar_full, g * 2 + (u & 1)), (u >> 1) & 1);
             }
         __syncwarp();
-    } else {
+    } else if (warp < kEpiWarp) {
         // ------------------------------------------------------ decoders
-        const int dw = warp - 1, g = dw >> 2;
+        const int dw = warp - 4, g = dw >> 2;
         const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
         const int tau = lane >> 4;
-        const bool valid = tau == 0 || has1;
         RowDecoder dec;
         dec.init(tables, lane, q, p.start_exp);
         // This thread's row of the group's A tile: MMA row m = 32*q + lane
         // (= accumulator lane), 128-byte swizzled.
-        const uint32_t m = uint32_t(32 * q + lane);
-        const uint32_t arow = sbase + p.off_a + (m >> 3) * 1024u +
-                              (m & 7u) * 128u;
-        const uint32_t swz = (m & 7u) << 4;
-        const int nu = nk > g ? (nk - g + NDG - 1) / NDG : 0;  // slices of this group
-        uint32_t out[32];
-        RareState rs;
+        const uint32_t mr = uint32_t(32 * q + lane);
+        const uint32_t arow = sbase + p.off_a + (mr >> 3) * 1024u + (mr & 7u) * 128u;
+        const uint32_t swz = (mr & 7u) << 4;
+        const int na = p.abuf * NDG;
         bool ok = ptx::mbar_wait(bar_tab, 0);
-        for (int u = 0; u < nu; ++u) {
+
+        // Position of the group's step t, advanced without divisions.
+        int k = t_begin - unit0 * kt + g, rb = unit0 % rbs;
+        while (k >= kt) {
+            k -= kt;
+            if (++rb == rbs) rb = 0;
+        }
+        int a = g, ause = 0;  // A tile t % na and its use t / na
+        for (int t = g, u = 0; t < nsteps; t += NDG, ++u) {
+            const bool valid = tau == 0 || 2 * rb + 1 < p.row_tiles;
             const int sidx = g * 2 + (u & 1);
             const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
             ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), (u >> 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
+            uint32_t out[32];
+            RareState rs;
             dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
                        slot + L.med + uint32_t(tau) * 32u, slot + (tau ? L.common1 : L.common0),
                        cap_c, cap_r, out, rs);
@@ -308,14 +374,11 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
 #pragma unroll
                 for (int w = 0; w < 32; ++w) out[w] = 0;
             }
-            // The A tile is free once the MMAs of the group's previous slice
-            // finished reading it.
-            // A tile a = g + NDG * (u % abuf), use u / abuf.
-            const int ashift = p.abuf - 1;
-            const int a = g + (u & ashift) * NDG, ause = u >> ashift;
+            // A tile a = t % na is free once the MMAs of step t - na finished.
             if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
-            dec.store(arow + uint32_t(a) * kATileBytes, swz, out, rs, slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
+            dec.store(arow + uint32_t(a) * kATileBytes, swz, out, rs,
+                      slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
             // Generic-proxy stores must be visible to the tensor cores.
             ptx::fence_proxy_async_smem();
             __syncwarp();
@@ -323,69 +386,134 @@ __global__ void __launch_bounds__(128 + 128 * NDG, 1)
                 ptx::mbar_arrive(bar_addr(bar_free, sidx));  // slot fully read
                 ptx::mbar_arrive(bar_addr(bar_afull, a));
             }
+            if ((a += NDG) >= na) a -= na, ++ause;
+            for (k += NDG; k >= kt;) {
+                k -= kt;
+                if (++rb == rbs) rb = 0;
+            }
+        }
+    } else {
+        // ------------------------------------------------------ epilogue
+        // Segment s (unit unit0 + s) is in accumulator s & 1. Whole units:
+        // TMEM -> BF16 -> y. Partial units: TMEM -> this CTA's FP32 partial
+        // pieces, release the accumulator, count the arrivals; the last
+        // arrival of a piece sums its partials in K order and stores it.
+        const int q = warp & 3;  // TMEM lane quarter
+        const int chunks = p.bn / 16;
+        const int row = 32 * q + lane;  // TMEM lane = slot in the unit's 128-row tile
+        // Output and workspace writes must not race the kernels this one
+        // depends on (they may still read those buffers).
+        ptx::wait_prerequisites();
+        auto store_row = [&](int nb, int c, int mrow, const float (&acc)[16]) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int n = nb * p.bn + 16 * c + j;
+                if (n < p.n)
+                    p.y[size_t(n) * p.m + mrow] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[j]));
+            }
+        };
+        for (int s = 0; s < nseg; ++s) {
+            const int b = s & 1;
+            const bool dok = ptx::mbar_wait(bar_addr(bar_d, b), uint32_t(s >> 1) & 1u);
+            ptx::tc_fence_after();
+            const int unit = unit0 + s, rb = unit % rbs, nb = unit / rbs;
+            const int ubeg = unit * kt;
+            const bool whole = t_begin <= ubeg && ubeg + kt <= t_end;
+            const int mrow = rb * 128 + lane_row(row);
+            const bool row_ok = mrow < p.m;
+            const uint32_t tbase = tmem + (uint32_t(32 * q) << 16) + uint32_t(b) * p.tmem_cols;
+            if (whole) {
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t v[16];
+                    ptx::tmem_ld_32x32b_x16(tbase + 16u * c, v);
+                    ptx::tmem_wait_ld();
+                    float acc[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] = dok ? __uint_as_float(v[j]) : 0.f;
+                    if (row_ok) store_row(nb, c, mrow, acc);
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));
+                continue;
+            }
+            // Partial segments are a CTA's first or last: slot `which`.
+            const int which = s > 0 ? 1 : 0;
+            const size_t piece0 = size_t(q) * size_t(chunks);  // this quarter's pieces
+            float* mine = p.ws_partials +
+                          ((size_t(cta) * 2 + size_t(which)) * size_t(p.pieces) + piece0) * 512u +
+                          size_t(lane) * 16u;
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t v[16];
+                ptx::tmem_ld_32x32b_x16(tbase + 16u * c, v);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                    ptx::stg_cg_f4(mine + size_t(c) * 512u + j,
+                                   dok ? make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                     __uint_as_float(v[j + 2]),
+                                                     __uint_as_float(v[j + 3]))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f));
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));  // TMEM read
+            __threadfence();  // partials visible before the arrivals count
+            __syncwarp();
+            const int c0 = step_owner(ubeg, p);
+            const int parts = step_owner(ubeg + kt - 1, p) - c0 + 1;
+            uint32_t* counters = p.ws_counters + size_t(unit) * size_t(p.pieces) + piece0;
+            // Lane c counts this CTA's arrival at piece c.
+            const uint32_t prior = lane < chunks ? atomicAdd(counters + lane, 1u) : 0u;
+            const uint32_t last = __ballot_sync(kFullMask, lane < chunks && prior == uint32_t(parts - 1));
+            if (!last) continue;
+            __threadfence();  // every partial of those pieces is visible now
+            for (uint32_t todo = last; todo; todo &= todo - 1) {
+                const int c = __ffs(todo) - 1;
+                // Partial pp of the piece: CTA c0 + pp, slot 1 only when the
+                // unit starts inside that CTA's range after its first segment.
+                auto partial = [&](int pp) {
+                    const int cp = c0 + pp;
+                    const int wh = (pp == 0 && step_start(cp, p) < ubeg) ? 1 : 0;
+                    return p.ws_partials +
+                           ((size_t(cp) * 2 + size_t(wh)) * size_t(p.pieces) + piece0 +
+                            size_t(c)) * 512u + size_t(lane) * 16u;
+                };
+                float acc[16];
+                // Two partials' loads in flight per round trip; sums in K order.
+#pragma unroll
+                for (int h = 0; h < 16; h += 8) {
+                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+                    for (int pp = 0; pp < parts; pp += 2) {
+                        const float* s0 = partial(pp) + h;
+                        const float4 x0 = ptx::ldg_cg_f4(s0), x1 = ptx::ldg_cg_f4(s0 + 4);
+                        float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
+                        if (pp + 1 < parts) {
+                            const float* s1 = partial(pp + 1) + h;
+                            y0 = ptx::ldg_cg_f4(s1), y1 = ptx::ldg_cg_f4(s1 + 4);
+                        }
+                        a0.x += x0.x, a0.y += x0.y, a0.z += x0.z, a0.w += x0.w;
+                        a1.x += x1.x, a1.y += x1.y, a1.z += x1.z, a1.w += x1.w;
+                        if (pp + 1 < parts) {
+                            a0.x += y0.x, a0.y += y0.y, a0.z += y0.z, a0.w += y0.w;
+                            a1.x += y1.x, a1.y += y1.y, a1.z += y1.z, a1.w += y1.w;
+                        }
+                    }
+                    acc[h] = a0.x, acc[h + 1] = a0.y, acc[h + 2] = a0.z, acc[h + 3] = a0.w;
+                    acc[h + 4] = a1.x, acc[h + 5] = a1.y, acc[h + 6] = a1.z, acc[h + 7] = a1.w;
+                }
+                if (row_ok) store_row(nb, c, mrow, acc);
+            }
+            __syncwarp();
+            if ((last >> lane) & 1u)
+                *reinterpret_cast<volatile uint32_t*>(counters + lane) = 0u;  // ready for reuse
         }
     }
 
-    // ---------------------------------------------------------- epilogue
-    float* red = reinterpret_cast<float*>(smem + p.off_a);  // [bn][128] FP32 when S > 1
-    if (warp >= 1 && warp <= 4 * NDG) {
-        const int g = (warp - 1) >> 2, q = warp & 3;
-        const bool dok = ptx::mbar_wait(bar_d, 0);
-        ptx::tc_fence_after();
-        const int row = 32 * q + lane;  // TMEM lane = slot in the reduction tile
-        const int mrow = mblk * 128 + lane_row(row);
-        const bool row_ok = mrow < p.m;
-        for (int c = g; c < p.bn / 16; c += NDG) {
-            uint32_t v[16];
-            ptx::tmem_ld_32x32b_x16(tmem + (uint32_t(32 * q) << 16) + 16u * c, v);
-            ptx::tmem_wait_ld();
-            if (nk == 0 || !dok) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = 0;
-            }
-            if (S == 1) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = nblk * p.bn + 16 * c + j;
-                    if (n < p.n && row_ok)
-                        p.y[size_t(n) * p.m + mrow] =
-                            __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[j])));
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) red[(16 * c + j) * 128 + row] = __uint_as_float(v[j]);
-            }
-        }
-        ptx::tc_fence_before();
-    }
-    if (S > 1) {
-        ptx::cluster_sync();
-        const int groups = p.bn * 32;  // float4 = 4 consecutive rows of one token
-        const int g0 = int(int64_t(groups) * rank / S), g1 = int(int64_t(groups) * (rank + 1) / S);
-        const uint32_t red_addr = ptx::smem_addr(red);
-        for (int gi = g0 + tid; gi < g1; gi += blockDim.x) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int src = 0; src < S; ++src) {
-                const float4 v = ptx::ld_cluster_f4(ptx::map_to_rank(red_addr + 16u * gi, src));
-                acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
-            }
-            const int n = nblk * p.bn + (gi >> 5);
-            const int mrow = mblk * 128 + lane_row((gi & 31) * 4);  // 4 slots = 4 consecutive rows
-            if (n < p.n && mrow < p.m) {
-                uint2 packed;
-                packed.x = uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(acc.x))) |
-                           (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(acc.y))) << 16);
-                packed.y = uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(acc.z))) |
-                           (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(acc.w))) << 16);
-                *reinterpret_cast<uint2*>(p.y + size_t(n) * p.m + mrow) = packed;
-            }
-        }
-        ptx::cluster_sync();  // partners may still read this CTA's tile until here
-    }
     __syncthreads();
     if (warp == 0) {
         ptx::tc_fence_after();
-        ptx::tmem_dealloc(tmem, p.tmem_cols);
+        ptx::tmem_dealloc(tmem, 2 * p.tmem_cols);
     }
 }
 
@@ -549,31 +677,6 @@ bool encode_plane_maps(PlaneMaps* maps, const void* b1, const void* b2, const vo
 
 static int tile_n(int n) { return n > 256 ? 256 : std::max(16, (n + 15) / 16 * 16); }
 
-static int active_clusters(int device, int size, uint32_t smem) {
-    DeviceInfo& d = device_info(device);
-    if (size <= 0 || size > 16) return 0;
-    if (d.active_clusters[size]) return d.active_clusters[size];
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(size * 64, 1, 1);
-    cfg.blockDim = dim3(gemm_threads(4), 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = size;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, zipgemm_kernel<4>, &cfg) != cudaSuccess ||
-        clusters <= 0) {
-        cudaGetLastError();
-        clusters = std::max(1, d.sms / size);
-    }
-    d.active_clusters[size] = clusters;
-    return clusters;
-}
-
 static cudaError_t ensure_gemm_attributes(int device) {
     DeviceInfo& d = device_info(device);
     if (d.gemm_attr) return cudaSuccess;
@@ -582,8 +685,6 @@ static cudaError_t ensure_gemm_attributes(int device) {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      d.smem_optin);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     }
     if (e == cudaSuccess) d.gemm_attr = true;
     else {
@@ -595,33 +696,119 @@ static cudaError_t ensure_gemm_attributes(int device) {
     return e;
 }
 
+// The persistent schedule of one launch (see the kernel's work schedule).
+struct Schedule {
+    int bn, row_blocks, units, steps, grid, pieces;
+    bool partial;  // some CTA range splits a unit: the fixup workspace is used
+};
+
+static Schedule make_schedule(int m, int n, int k, int kparts, int sms) {
+    Schedule s{};
+    const int kt = k / 64;
+    s.bn = tile_n(n);
+    s.row_blocks = (m / 64 + 1) / 2;
+    s.units = s.row_blocks * ((n + s.bn - 1) / s.bn);
+    s.steps = s.units * kt;
+    const int64_t want = kparts > 0 ? int64_t(s.units) * kparts : int64_t(std::max(1, sms));
+    s.grid = int(std::max<int64_t>(1, std::min<int64_t>(want, s.steps)));
+    s.pieces = s.bn / 4;
+    s.partial = false;
+    for (int c = 1; c < s.grid && !s.partial; ++c)
+        if ((int64_t(c) * s.steps / s.grid) % kt) s.partial = true;
+    return s;
+}
+
+// Fixup scratch of a schedule: FP32 partial tiles (any contents) and one
+// arrival counter per unit piece. Counters live in their own buffer, which
+// holds zeros between launches (a launch returns every counter it used to
+// zero), so launches of different shapes can share both buffers.
+static size_t schedule_partial_bytes(const Schedule& s) {
+    return s.partial ? size_t(s.grid) * 2u * size_t(s.pieces) * 512u * sizeof(float) : 0;
+}
+static size_t schedule_counter_bytes(const Schedule& s) {
+    return s.partial ? (size_t(s.units) * size_t(s.pieces) * 4u + 15u) / 16u * 16u : 0;
+}
+
+// Library-owned fixup scratch, one pair of buffers per (device, stream):
+// launches on one stream are ordered, so they can share it. Grown (never
+// shrunk) on demand; growth is refused while the stream is being captured.
+struct WorkspaceEntry {
+    int device;
+    cudaStream_t stream;
+    void* partials;
+    size_t partial_bytes;
+    void* counters;
+    size_t counter_bytes;
+};
+std::vector<WorkspaceEntry> g_workspaces;
+std::mutex g_workspace_mutex;
+
+static cudaError_t library_workspace(int device, cudaStream_t stream, size_t partial_bytes,
+                                     size_t counter_bytes, void** partials, void** counters) {
+    std::lock_guard<std::mutex> lock(g_workspace_mutex);
+    WorkspaceEntry* entry = nullptr;
+    for (WorkspaceEntry& e : g_workspaces)
+        if (e.device == device && e.stream == stream) entry = &e;
+    if (!entry) {
+        g_workspaces.push_back({device, stream, nullptr, 0, nullptr, 0});
+        entry = &g_workspaces.back();
+    }
+    if (entry->partial_bytes < partial_bytes || entry->counter_bytes < counter_bytes) {
+        cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &status) != cudaSuccess ||
+            status != cudaStreamCaptureStatusNone) {
+            zs_set_error("zipgemm: K-range scratch must be allocated outside stream capture "
+                         "(run this shape once on the stream before capturing it)");
+            return cudaErrorStreamCaptureUnsupported;
+        }
+        // Launches already queued may still use the old buffers.
+        cudaError_t e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        if (entry->partial_bytes < partial_bytes) {
+            cudaFree(entry->partials);
+            entry->partials = nullptr, entry->partial_bytes = 0;
+            if ((e = cudaMalloc(&entry->partials, partial_bytes)) != cudaSuccess) {
+                zs_set_error("zipgemm: could not allocate K-range scratch");
+                return e;
+            }
+            entry->partial_bytes = partial_bytes;
+        }
+        if (entry->counter_bytes < counter_bytes) {
+            cudaFree(entry->counters);
+            entry->counters = nullptr, entry->counter_bytes = 0;
+            if ((e = cudaMalloc(&entry->counters, counter_bytes)) != cudaSuccess) {
+                zs_set_error("zipgemm: could not allocate K-range counters");
+                return e;
+            }
+            if ((e = cudaMemsetAsync(entry->counters, 0, counter_bytes, stream)) != cudaSuccess)
+                return e;
+            entry->counter_bytes = counter_bytes;
+        }
+    }
+    *partials = entry->partials;
+    *counters = entry->counters;
+    return cudaSuccess;
+}
+
 int plan_kparts(int m, int n, int k, int device) {
     if (!valid_matrix(m, k) || n <= 0) return -1;
-    DeviceInfo& d = device_info(device);
-    if (ensure_gemm_attributes(device) != cudaSuccess) return 1;
-    const int kt = k / 64;
-    const int units = ((m / 64 + 1) / 2) * ((n + 255) / 256);
-    const int max_s = std::min(kt, 16);
-    int best = 1;
-    double best_cost = 1e300;
-    for (int s = 1; s <= max_s; ++s) {
-        const int slots = active_clusters(device, s, uint32_t(d.smem_optin)) * s;
-        if (slots <= 0) continue;
-        const int ctas = units * s;
-        const int waves = (ctas + slots - 1) / slots;
-        // Per CTA: its K slices plus a fixed start-up/reduction overhead
-        // (about four slices); a partially filled wave still costs a wave.
-        const double per_cta = double((kt + s - 1) / s) + 4.0 + (s > 1 ? 1.0 : 0.0);
-        const double cost = waves * per_cta * (s > 8 ? 1.03 : 1.0);
-        if (cost < best_cost - 1e-9) best_cost = cost, best = s;
-    }
-    return best;
+    const Schedule s = make_schedule(m, n, k, 0, device_info(device).sms);
+    return std::max(1, s.grid / s.units);
+}
+
+void gemm_workspace_bytes(int m, int n, int k, int kparts, int device, size_t* partial_bytes,
+                          size_t* counter_bytes) {
+    *partial_bytes = *counter_bytes = 0;
+    if (!valid_matrix(m, k) || n <= 0) return;
+    const Schedule s = make_schedule(m, n, k, kparts, device_info(device).sms);
+    *partial_bytes = schedule_partial_bytes(s);
+    *counter_bytes = schedule_counter_bytes(s);
 }
 
 cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
                            const void* b2, const void* b3, const void* medium, const void* global,
                            int max_common, int max_rare, int start_exp, const void* x, void* y,
-                           int m, int n, int k, int kparts) {
+                           int m, int n, int k, int kparts, const GemmScratch* scratch) {
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return e;
@@ -629,8 +816,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     DeviceInfo& d = device_info(device);
     if ((e = ensure_gemm_attributes(device)) != cudaSuccess) return e;
     const int kt = k / 64;
-    if (kparts <= 0) kparts = plan_kparts(m, n, k, device);
-    kparts = std::max(1, std::min({kparts, kt, 16}));
+    const Schedule sched = make_schedule(m, n, k, std::max(0, kparts), d.sms);
 
     GemmParams p{};
     p.sm = static_cast<const uint8_t*>(sm);
@@ -638,8 +824,28 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.global = static_cast<const int*>(global);
     p.y = static_cast<uint16_t*>(y);
     p.m = m, p.n = n, p.k = k, p.kt = kt, p.row_tiles = m / 64;
-    p.kparts = kparts;
-    p.bn = tile_n(n);
+    p.row_blocks = sched.row_blocks, p.units = sched.units, p.steps = sched.steps;
+    p.grid = sched.grid, p.pieces = sched.pieces;
+    p.bn = sched.bn;
+    if (sched.partial) {
+        const size_t need_p = schedule_partial_bytes(sched), need_c = schedule_counter_bytes(sched);
+        void *partials = nullptr, *counters = nullptr;
+        if (scratch) {
+            if (!scratch->partials || !scratch->counters || scratch->partial_bytes < need_p ||
+                scratch->counter_bytes < need_c ||
+                ((reinterpret_cast<uintptr_t>(scratch->partials) |
+                  reinterpret_cast<uintptr_t>(scratch->counters)) & 15u)) {
+                zs_set_error("zipgemm: caller scratch missing, too small or not 16-byte aligned");
+                return cudaErrorInvalidValue;
+            }
+            partials = scratch->partials, counters = scratch->counters;
+        } else if ((e = library_workspace(device, stream, need_p, need_c, &partials,
+                                          &counters)) != cudaSuccess) {
+            return e;
+        }
+        p.ws_counters = static_cast<uint32_t*>(counters);
+        p.ws_partials = static_cast<float*>(partials);
+    }
     p.cap_c = common_capacity(max_common);
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
@@ -689,14 +895,11 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
         zs_set_error("zipgemm: packed payload capacity leaves no room for the shared-memory rings");
         return cudaErrorInvalidConfiguration;
     }
-    // Split-K reduction reuses the A tiles and rings: they must hold a
-    // bn x 128 FP32 tile.
-    if (kparts > 1 && uint32_t(p.bn) * 128 * 4 > l.total - kRingPadBytes - l.off_a)
-        kparts = p.kparts = 1;
     p.nx = l.nx;
     p.off_a = l.off_a, p.off_x = l.off_x;
     p.off_slots = l.off_slots, p.x_bytes = l.x_bytes, p.slot = l.slot;
-    // TMEM holds only the FP32 accumulator (bn columns).
+    // TMEM holds two FP32 accumulators of bn columns (consecutive segments
+    // alternate, so one can drain while the next accumulates).
     uint32_t cols = 32;
     while (cols < uint32_t(p.bn)) cols <<= 1;
     p.tmem_cols = cols;
@@ -714,15 +917,16 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     }
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(((m / 64 + 1) / 2) * kparts), unsigned((n + p.bn - 1) / p.bn), 1);
+    cfg.gridDim = dim3(unsigned(sched.grid), 1, 1);
     cfg.blockDim = dim3(gemm_threads(ndg), 1, 1);
     cfg.dynamicSmemBytes = l.total;
     cfg.stream = stream;
+    // Programmatic dependent launch: the prologue and the first weight
+    // copies overlap the previous kernel's tail; x is read and the output
+    // written only after it completes (griddepcontrol.wait in the kernel).
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = unsigned(kparts);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = ndg == 4   ? cudaLaunchKernelEx(&cfg, zipgemm_kernel<4>, xmap, pm, mmap, p)
@@ -731,10 +935,8 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     if (e != cudaSuccess) {
         char msg[220];
         snprintf(msg, sizeof(msg),
-                 "zipgemm launch (grid %u x %u, cluster %d, %u B shared, %d decoder groups, "
-                 "%d x slots, bn %d): %s",
-                 cfg.gridDim.x, cfg.gridDim.y, kparts, l.total, ndg, l.nx, p.bn,
-                 cudaGetErrorString(e));
+                 "zipgemm launch (grid %u, %u B shared, %d decoder groups, %d x slots, bn %d): %s",
+                 cfg.gridDim.x, l.total, ndg, l.nx, p.bn, cudaGetErrorString(e));
         zs_set_error(msg);
     }
     return e;

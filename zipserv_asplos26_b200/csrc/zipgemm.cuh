@@ -37,10 +37,16 @@ struct GemmParams {
     const uint16_t* rare;
     const int* global;
     uint16_t* y;           // [n, m] BF16
+    float* ws_partials;    // [grid][2][pieces][32 lanes][16] FP32 partial tiles
+    uint32_t* ws_counters;  // [units][pieces] arrivals (zero between launches)
     int m, n, k;
     int kt;                // k / 64
     int row_tiles;         // m / 64
-    int kparts;            // CTAs per cluster along K
+    int row_blocks;        // 128-row blocks: ceil(row_tiles / 2)
+    int units;             // row_blocks * n blocks
+    int steps;             // units * kt: the (unit, K slice) work items
+    int grid;              // CTAs; CTA c owns items [c*steps/grid, (c+1)*steps/grid)
+    int pieces;            // 32-row x 16-column pieces of a unit's tile: 4 * bn / 16
     int bn;                // N tile (multiple of 16, <= 256)
     int nx;                // x ring slots
     int abuf;              // decoded A tiles per decoder group (1 or 2)
@@ -50,7 +56,7 @@ struct GemmParams {
     uint32_t off_a, off_x, off_slots;
     uint32_t x_bytes;      // one x slot: bn tokens x one K slice (bn * 128 bytes)
     SlotLayout slot;       // one K slice of the block's two tile rows
-    uint32_t tmem_cols;
+    uint32_t tmem_cols;    // columns of one accumulator (two are allocated)
 };
 
 struct DecompressParams {
@@ -77,13 +83,27 @@ struct PlaneMaps {
     int count;
 };
 
-// Launch the fused kernel; `kparts` = 0 selects the partition. Arguments are
-// assumed validated.
+// Caller-owned K-range fixup scratch: FP32 partial tiles (any contents) and
+// arrival counters (zero-filled before their first use; every launch returns
+// the counters it used to zero).
+struct GemmScratch {
+    void* partials;
+    size_t partial_bytes;
+    void* counters;
+    size_t counter_bytes;
+};
+
+// Launch the fused kernel. `kparts` = 0: one CTA per SM (or fewer for small
+// problems); kparts > 0: kparts CTAs per 128-row block. `scratch` null: the
+// library's own per-stream scratch. Arguments are assumed validated.
 cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
                            const void* b2, const void* b3, const void* medium, const void* global,
                            int max_common, int max_rare, int start_exp, const void* x, void* y,
-                           int m, int n, int k, int kparts);
+                           int m, int n, int k, int kparts, const GemmScratch* scratch = nullptr);
 int plan_kparts(int m, int n, int k, int device);
+// Scratch the launch needs (both 0 when no CTA range splits a row block).
+void gemm_workspace_bytes(int m, int n, int k, int kparts, int device, size_t* partial_bytes,
+                          size_t* counter_bytes);
 
 cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* rare,
                               const void* b1, const void* b2, const void* b3,

@@ -80,6 +80,13 @@ def _library() -> ctypes.CDLL:
         lib.zipserv_mm_plan.restype = integer
         lib.zipserv_device_flags.argtypes = [ctypes.POINTER(ctypes.c_uint), integer]
         lib.zipserv_device_flags.restype = integer
+    if hasattr(lib, "zipserv_mm_ws"):
+        u64 = ctypes.c_uint64
+        lib.zipserv_mm_ws.argtypes = ([ptr] * 8 + [integer] * 3 + [ptr] * 2 + [integer] * 4 +
+                                      [ptr, u64, ptr, u64])
+        lib.zipserv_mm_ws.restype = integer
+        lib.zipserv_mm_workspace_size.argtypes = [integer] * 4 + [ctypes.POINTER(u64)] * 2
+        lib.zipserv_mm_workspace_size.restype = integer
     return lib
 
 
@@ -272,9 +279,23 @@ def linear(x: Tensor, packed: PackedWeight, *, split_k: int = 1,
                    packed.max_rare, packed.start_exp, split_k, partial_dtype == "fp32")
 
 
+def workspace_size(m: int, n: int, k: int, k_parts: int = 0) -> tuple[int, int]:
+    """(partial bytes, counter bytes) of scratch ``linear_kparts(...,
+    workspace=...)`` needs on the current GPU; (0, 0) when none."""
+    part, ctr = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    _check(_cuda_library().zipserv_mm_workspace_size(m, n, k, k_parts, ctypes.byref(part),
+                                                     ctypes.byref(ctr)))
+    return int(part.value), int(ctr.value)
+
+
 def linear_kparts(x: Tensor, packed: PackedWeight, k_parts: int,
-                  out: Tensor | None = None) -> Tensor:
-    """``linear`` with an explicit in-kernel K partition (0 = automatic)."""
+                  out: Tensor | None = None,
+                  workspace: tuple[Tensor, Tensor] | None = None) -> Tensor:
+    """``linear`` with an explicit K partition (0 = the default schedule):
+    k_parts CTAs per 128-row block. ``workspace`` = (partials, counters),
+    CUDA byte tensors at least ``workspace_size`` long, the counters
+    zero-filled once (calls leave them zeroed; calls must not overlap),
+    replaces the library's own per-stream scratch."""
     m, k = packed.m, packed.k
     if x.dtype != torch.bfloat16 or x.shape[-1] != k:
         raise ValueError("ZipServ linear requires BF16 activations with the matching input width")
@@ -288,15 +309,28 @@ def linear_kparts(x: Tensor, packed: PackedWeight, k_parts: int,
     if n:
         _gemm_limits(m, n, k, 1)
         lib = _cuda_library()
-        _check(lib.zipserv_mm_kparts(torch.cuda.current_stream(x.device).cuda_stream,
-                                     *(b.data_ptr() for b in packed.buffers), packed.max_common,
-                                     packed.max_rare, packed.start_exp, flat.data_ptr(),
-                                     out.data_ptr(), m, n, k, k_parts))
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        ptrs = [b.data_ptr() for b in packed.buffers]
+        if workspace is None:
+            _check(lib.zipserv_mm_kparts(stream, *ptrs, packed.max_common, packed.max_rare,
+                                         packed.start_exp, flat.data_ptr(), out.data_ptr(),
+                                         m, n, k, k_parts))
+        else:
+            partials, counters = workspace
+            if partials.device != x.device or counters.device != x.device:
+                raise ValueError("workspace must be on the activations' device")
+            _check(lib.zipserv_mm_ws(stream, *ptrs, packed.max_common, packed.max_rare,
+                                     packed.start_exp, flat.data_ptr(), out.data_ptr(), m, n, k,
+                                     k_parts, partials.data_ptr(),
+                                     partials.numel() * partials.element_size(),
+                                     counters.data_ptr(),
+                                     counters.numel() * counters.element_size()))
     return out.reshape(*x.shape[:-1], m)
 
 
 def plan_kparts(m: int, n: int, k: int) -> int:
-    """The K partition the fused kernel uses for this shape on the current GPU."""
+    """CTAs per 128-row block of the default schedule on the current GPU
+    (at least 1; the persistent grid may also give a CTA several blocks)."""
     return int(_cuda_library().zipserv_mm_plan(m, n, k))
 
 
