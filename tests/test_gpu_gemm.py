@@ -235,10 +235,13 @@ def test_unequally_spaced_bitmaps(native_lib, oracle_mod, m, k):
 
 
 @pytest.mark.parametrize("m,k,n,kparts", [(640, 1024, 40, 3), (256, 1024, 600, 5),
-                                          (192, 4096, 16, 0), (64, 64, 1, 0)])
+                                          (192, 4096, 16, 0), (64, 64, 1, 0),
+                                          (4096, 1024, 8, 8), (4160, 1024, 24, 16)])
 def test_split_rows_exact(native_lib, oracle_mod, m, k, n, kparts):
     """Uneven CTA ranges: CTAs whose first and last row blocks are both split,
-    several N tiles, row blocks with one tile row; integer operands, exact."""
+    several N tiles, row blocks with one tile row; grids larger than the GPU
+    (reduced by the last CTA to arrive instead of a waiting first part);
+    integer operands, exact."""
     rng = oracle_mod.MT19937(m + k + n)
     w = oracle_mod.integer_matrix(rng, m * k).reshape(m, k)
     x = oracle_mod.integer_matrix(rng, n * k).reshape(n, k)

@@ -69,6 +69,31 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+// Bounded wait until the global word at `p` (written by other CTAs with
+// release semantics) reaches `value`: acquire loads, two-second limit, then
+// sets g_device_flags bit 0 and returns false.
+__device__ __forceinline__ bool wait_global_geq(const uint32_t* p, uint32_t value) {
+    uint64_t start = 0;
+    for (uint32_t i = 0; i < (1u << 30); ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= value) return true;
+        if ((i & 15) == 15) {
+            const uint64_t now = global_timer_ns();
+            if (!start) start = now;
+            else if (now - start > 2000000000ull) break;
+            __nanosleep(64);
+        }
+    }
+    atomicOr(&g_device_flags, 1u);
+    return false;
+}
+// Release increment of a global counter (orders this thread's earlier writes
+// before the increment for any CTA that acquires the counter).
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // ------------------------------------------------------------- async copies
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
 // dst and src 16-byte aligned, bytes a positive multiple of 16.

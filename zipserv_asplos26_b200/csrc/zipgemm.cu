@@ -440,6 +440,71 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             // Partial segments are a CTA's first or last: slot `which`.
             const int which = s > 0 ? 1 : 0;
             const size_t piece0 = size_t(q) * size_t(chunks);  // this quarter's pieces
+            const int c0 = step_owner(ubeg, p);
+            const int parts = step_owner(ubeg + kt - 1, p) - c0 + 1;
+            // Partial pp of a piece: CTA c0 + pp, slot 1 only when the unit
+            // starts inside that CTA's range after its first segment.
+            auto partial = [&](int pp, int c) {
+                const int cp = c0 + pp;
+                const int wh = (pp == 0 && step_start(cp, p) < ubeg) ? 1 : 0;
+                return p.ws_partials +
+                       ((size_t(cp) * 2 + size_t(wh)) * size_t(p.pieces) + piece0 + size_t(c)) *
+                           512u +
+                       size_t(lane) * 16u;
+            };
+            // acc += partials first .. parts - 1 of piece c, two loads in
+            // flight per round trip, summed in K order.
+            auto add_partials = [&](int c, int first, float (&acc)[16]) {
+#pragma unroll
+                for (int h = 0; h < 16; h += 8) {
+                    float4 a0 = make_float4(acc[h], acc[h + 1], acc[h + 2], acc[h + 3]);
+                    float4 a1 = make_float4(acc[h + 4], acc[h + 5], acc[h + 6], acc[h + 7]);
+                    for (int pp = first; pp < parts; pp += 2) {
+                        const float* s0 = partial(pp, c) + h;
+                        const float4 x0 = ptx::ldg_cg_f4(s0), x1 = ptx::ldg_cg_f4(s0 + 4);
+                        float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
+                        if (pp + 1 < parts) {
+                            const float* s1 = partial(pp + 1, c) + h;
+                            y0 = ptx::ldg_cg_f4(s1), y1 = ptx::ldg_cg_f4(s1 + 4);
+                        }
+                        a0.x += x0.x, a0.y += x0.y, a0.z += x0.z, a0.w += x0.w;
+                        a1.x += x1.x, a1.y += x1.y, a1.z += x1.z, a1.w += x1.w;
+                        if (pp + 1 < parts) {
+                            a0.x += y0.x, a0.y += y0.y, a0.z += y0.z, a0.w += y0.w;
+                            a1.x += y1.x, a1.y += y1.y, a1.z += y1.z, a1.w += y1.w;
+                        }
+                    }
+                    acc[h] = a0.x, acc[h + 1] = a0.y, acc[h + 2] = a0.z, acc[h + 3] = a0.w;
+                    acc[h + 4] = a1.x, acc[h + 5] = a1.y, acc[h + 6] = a1.z, acc[h + 7] = a1.w;
+                }
+            };
+            if (p.resident && cta == c0) {
+                // This CTA holds the unit's first K part, the last one it
+                // computes: it reduces the unit once the other parts (each
+                // their CTA's first segment, so never waiting on this one)
+                // have published their quarter-q pieces.
+                uint32_t* quarter = p.ws_counters + size_t(unit) * 4u + size_t(q);
+                bool wok = true;
+                if (lane == 0) wok = ptx::wait_global_geq(quarter, uint32_t(parts - 1));
+                wok = __shfl_sync(kFullMask, wok, 0);
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t v[16];
+                    ptx::tmem_ld_32x32b_x16(tbase + 16u * c, v);
+                    ptx::tmem_wait_ld();
+                    float acc[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) acc[j] = dok ? __uint_as_float(v[j]) : 0.f;
+                    if (wok) add_partials(c, 1, acc);
+                    if (row_ok) store_row(nb, c, mrow, acc);
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    ptx::mbar_arrive(bar_addr(bar_tempty, b));
+                    *reinterpret_cast<volatile uint32_t*>(quarter) = 0u;  // ready for reuse
+                }
+                continue;
+            }
             float* mine = p.ws_partials +
                           ((size_t(cta) * 2 + size_t(which)) * size_t(p.pieces) + piece0) * 512u +
                           size_t(lane) * 16u;
@@ -460,8 +525,13 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));  // TMEM read
             __threadfence();  // partials visible before the arrivals count
             __syncwarp();
-            const int c0 = step_owner(ubeg, p);
-            const int parts = step_owner(ubeg + kt - 1, p) - c0 + 1;
+            if (p.resident) {
+                if (lane == 0)
+                    ptx::red_release_add(p.ws_counters + size_t(unit) * 4u + size_t(q), 1u);
+                continue;
+            }
+            // Not every CTA resident: whoever delivers a piece's last partial
+            // reduces it.
             uint32_t* counters = p.ws_counters + size_t(unit) * size_t(p.pieces) + piece0;
             // Lane c counts this CTA's arrival at piece c.
             const uint32_t prior = lane < chunks ? atomicAdd(counters + lane, 1u) : 0u;
@@ -470,38 +540,10 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             __threadfence();  // every partial of those pieces is visible now
             for (uint32_t todo = last; todo; todo &= todo - 1) {
                 const int c = __ffs(todo) - 1;
-                // Partial pp of the piece: CTA c0 + pp, slot 1 only when the
-                // unit starts inside that CTA's range after its first segment.
-                auto partial = [&](int pp) {
-                    const int cp = c0 + pp;
-                    const int wh = (pp == 0 && step_start(cp, p) < ubeg) ? 1 : 0;
-                    return p.ws_partials +
-                           ((size_t(cp) * 2 + size_t(wh)) * size_t(p.pieces) + piece0 +
-                            size_t(c)) * 512u + size_t(lane) * 16u;
-                };
                 float acc[16];
-                // Two partials' loads in flight per round trip; sums in K order.
 #pragma unroll
-                for (int h = 0; h < 16; h += 8) {
-                    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-                    for (int pp = 0; pp < parts; pp += 2) {
-                        const float* s0 = partial(pp) + h;
-                        const float4 x0 = ptx::ldg_cg_f4(s0), x1 = ptx::ldg_cg_f4(s0 + 4);
-                        float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
-                        if (pp + 1 < parts) {
-                            const float* s1 = partial(pp + 1) + h;
-                            y0 = ptx::ldg_cg_f4(s1), y1 = ptx::ldg_cg_f4(s1 + 4);
-                        }
-                        a0.x += x0.x, a0.y += x0.y, a0.z += x0.z, a0.w += x0.w;
-                        a1.x += x1.x, a1.y += x1.y, a1.z += x1.z, a1.w += x1.w;
-                        if (pp + 1 < parts) {
-                            a0.x += y0.x, a0.y += y0.y, a0.z += y0.z, a0.w += y0.w;
-                            a1.x += y1.x, a1.y += y1.y, a1.z += y1.z, a1.w += y1.w;
-                        }
-                    }
-                    acc[h] = a0.x, acc[h + 1] = a0.y, acc[h + 2] = a0.z, acc[h + 3] = a0.w;
-                    acc[h + 4] = a1.x, acc[h + 5] = a1.y, acc[h + 6] = a1.z, acc[h + 7] = a1.w;
-                }
+                for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+                add_partials(c, 0, acc);
                 if (row_ok) store_row(nb, c, mrow, acc);
             }
             __syncwarp();
@@ -826,6 +868,9 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.m = m, p.n = n, p.k = k, p.kt = kt, p.row_tiles = m / 64;
     p.row_blocks = sched.row_blocks, p.units = sched.units, p.steps = sched.steps;
     p.grid = sched.grid, p.pieces = sched.pieces;
+    // One CTA per SM (the shared-memory footprint allows no more): with at
+    // most one CTA per SM every CTA of the grid runs at the same time.
+    p.resident = sched.grid <= d.sms ? 1 : 0;
     p.bn = sched.bn;
     if (sched.partial) {
         const size_t need_p = schedule_partial_bytes(sched), need_c = schedule_counter_bytes(sched);

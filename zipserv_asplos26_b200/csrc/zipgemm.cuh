@@ -47,6 +47,8 @@ struct GemmParams {
     int steps;             // units * kt: the (unit, K slice) work items
     int grid;              // CTAs; CTA c owns items [c*steps/grid, (c+1)*steps/grid)
     int pieces;            // 32-row x 16-column pieces of a unit's tile: 4 * bn / 16
+    int resident;          // 1: every CTA runs at once (grid <= SMs), so the first
+                           // part's CTA may wait for a unit's other parts
     int bn;                // N tile (multiple of 16, <= 256)
     int nx;                // x ring slots
     int abuf;              // decoded A tiles per decoder group (1 or 2)
