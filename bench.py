@@ -160,7 +160,7 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         mm, kk, (r0, r1), (c0, c1) = _shard(name, m, k, split, world, rank)
         local = full[r0:r1, c0:c1].contiguous()
         packed = runtime.compress(local)
-        layers.append({"name": name, "m": mm, "k": kk, "split": split, "packed": packed.to(dev),
+        layers.append({"name": name, "m": mm, "k": kk, "split": split, "packed": packed,
                        "dense": local.to(dev), "storage": packed.storage_bytes})
         del full
     # Every call gets its own device copy of its weight (packed and dense), so
@@ -170,12 +170,8 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     calls = []
     for lay in layers:
         for n in args.tokens:
-            packed = lay["packed"]
-            copy = runtime.PackedWeight(tuple(b.clone() for b in packed.buffers), packed.m,
-                                        packed.k, packed.max_common, packed.max_rare,
-                                        packed.start_exp)
             calls.append({
-                "lay": lay, "n": n, "packed": copy, "dense": lay["dense"].clone(),
+                "lay": lay, "n": n, "packed": lay["packed"].to(dev), "dense": lay["dense"].clone(),
                 "x": torch.randn(n, lay["k"], generator=gen).to(torch.bfloat16).to(dev),
                 "out": torch.empty(n, lay["m"], dtype=torch.bfloat16, device=dev),
             })

@@ -641,9 +641,12 @@ int device_sm_count(int device) { return device_info(device).sms; }
 
 SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r) {
     // One K slice of two tile rows. A bitmap plane's tile occupies
-    // plane_pitch bytes (576: the tensor load's box is 72 words wide, the 8
-    // words past the 64-word tile zero-filled, which puts tile row 1 64
-    // bytes off modulo 128).
+    // plane_pitch bytes: the tensor load's box is wider than the 64-word
+    // tile (the words past it zero-filled), which puts tile row 1 off tile
+    // row 0 modulo 128 bytes, so the half-warps decoding the two tile rows
+    // read different banks (528: 16 bytes off, enough for the decoder's
+    // byte loads, which touch four banks per half-warp; 576: 64 bytes off,
+    // with every plane 128-byte aligned as separate tensor loads require).
     SlotLayout s{};
     s.plane1 = plane_pitch;
     s.plane_stride = 2u * plane_pitch;
@@ -894,11 +897,17 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.cap_c = common_capacity(max_common);
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
-    // Bitmap tensor maps: 72-word boxes (bank offset for tile row 1) when the
-    // driver accepts a box wider than the tile, else 64.
+    // Bitmap tensor maps. Equally spaced planes (one allocation, as the
+    // runtime lays them out) load with one 4-D copy into a 528-byte pitch;
+    // otherwise three copies need 128-byte aligned planes: pitch 576. 512
+    // (no bank offset) if the driver rejects a box wider than the tile.
     PlaneMaps pm;
-    uint32_t pitch = 576;
-    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 72, 1, 2)) {
+    const auto a1 = reinterpret_cast<uintptr_t>(b1), a2 = reinterpret_cast<uintptr_t>(b2),
+               a3 = reinterpret_cast<uintptr_t>(b3);
+    const bool spaced = a2 > a1 && a2 - a1 == a3 - a2 && (a2 - a1) % 16 == 0 &&
+                        a2 - a1 < (uint64_t(1) << 40);  // the test encode_plane_maps makes
+    uint32_t pitch = spaced ? 528 : 576;
+    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), pitch / 8, 1, 2)) {
         pitch = 512;
         if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 64, 1, 2)) {
             zs_set_error("zipgemm: bitmap tensor maps rejected (bitmaps must be 16-byte aligned)");
