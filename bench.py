@@ -19,7 +19,8 @@ the step through the public API (runtime.linear) with the activations copied
 from pinned host memory and the outputs copied back inside the timed region.
 cuBLAS BF16 on the dense weights is timed the same way. With --gpus N
 (torchrun), every linear is split Megatron-style: qkv/gate_up by output rows
-(no collective), o/down by K with an NCCL all-reduce of the BF16 partial outputs inside the timed region.
+(no collective), o/down by K with an NCCL all-reduce of the BF16 partial
+outputs inside the timed region.
 
 --impl reference times the reference's CPU implementation of the path (the
 restated decoder and FP32 GEMM of oracle/, all host threads) on the same
@@ -374,8 +375,9 @@ class _Null:
 
 def _traffic_record() -> dict:
     """DRAM bytes / algorithmic bytes of one ncu-captured ZipGEMM launch
-    (profiles/zipgemm_o16_traffic.txt, ``key: value`` lines)."""
-    path = ROOT / "profiles" / "zipgemm_o16_traffic.txt"
+    (profiles/zipgemm_gate_up16_traffic.txt, ``key: value`` lines: the
+    largest bench shape, whose packed weight exceeds L2)."""
+    path = ROOT / "profiles" / "zipgemm_gate_up16_traffic.txt"
     rec = {}
     if path.is_file():
         for line in path.read_text().splitlines():

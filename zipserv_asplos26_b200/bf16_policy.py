@@ -5,14 +5,16 @@ bf16_policy.py:14-134): the same names, dataclasses, argument meaning and
 rejection messages' purpose, so the linear method can call either. What is
 specific to this B200 library:
 
-* The fused kernel picks its own K partition (a thread-block cluster of up to
-  16 CTAs reduced in distributed shared memory), so ``split_k`` never needs a
-  workspace: candidates carry ``workspace_bytes = 0`` and the score models the
-  cluster partition instead of a separate reduction kernel.
-* Scores use a wave model of the kernel: one CTA per SM, a 128-row block per
-  CTA, N tiles of up to 128 tokens, and a fixed start-up cost of about three
-  K slices per CTA (measured on B200: ~3 us set-up against ~0.85 us per K
-  slice per SM).
+* The fused kernel schedules K itself (a persistent grid whose CTAs take
+  equal ranges of K slices; split row blocks are summed in FP32 inside the
+  kernel, in a fixed order), so ``split_k`` never needs a caller workspace:
+  candidates carry ``workspace_bytes = 0``. The split the planner returns
+  satisfies the native contract and is passed through; the kernel's own
+  schedule does not depend on it.
+* Scores model the reference's split choice on this kernel's cost shape: one
+  CTA per SM, a 128-row block per CTA, N tiles of up to 128 tokens, and a
+  fixed start-up cost of about three K slices per CTA (measured on B200: ~3 us
+  set-up against ~0.85 us per K slice per SM).
 
 Limits (``gemm_rejection``) follow csrc/CodecUtils.h:11-36 exactly: they are
 the contract the native entry points validate.
@@ -24,7 +26,7 @@ from functools import lru_cache
 
 INT32_MAX = 2**31 - 1
 GRID_Y_MAX = 65535
-MAX_CLUSTER = 16          # K partition limit of the fused kernel
+MAX_CLUSTER = 16          # largest explicit K partition the native API accepts
 STARTUP_SLICES = 3.0      # per-CTA fixed cost, in K-slice units (B200 measurement)
 
 
@@ -108,10 +110,10 @@ def token_tile(tokens: int) -> int:
 @lru_cache(maxsize=4096)
 def split_candidates(m: int, tokens: int, k: int, sms: int, workspace_bytes: int,
                      partial_bytes: int = 2) -> tuple[SplitCandidate, ...]:
-    """Every admissible split (a divisor of K/64 up to the kernel's cluster
-    limit, so the native Split-K contract holds) with its wave-model score
-    (lower is better): waves x (K slices per CTA + start-up). The kernel
-    reduces partitions in shared memory, so no workspace is used."""
+    """Every admissible split (a divisor of K/64 up to 16, so the native
+    Split-K contract holds) with its wave-model score (lower is better):
+    waves x (K slices per CTA + start-up). The kernel reduces K ranges
+    internally, so no caller workspace is used."""
     if type(sms) is not int or sms < 1 or partial_bytes not in (2, 4):
         raise ValueError("Require positive SM count and 2- or 4-byte partials")
     if type(workspace_bytes) is not int or workspace_bytes < 0:
@@ -126,7 +128,7 @@ def split_candidates(m: int, tokens: int, k: int, sms: int, workspace_bytes: int
         if slices % split or gemm_rejection(m, tokens, k, split):
             continue
         ctas = row_blocks * n_tiles * split
-        slots = (sms // split) * split  # whole clusters per wave
+        slots = (sms // split) * split  # whole split groups per wave
         if slots == 0:
             continue
         waves = -(-ctas // slots)

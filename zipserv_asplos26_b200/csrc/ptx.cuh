@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers, bulk/tensor async copies,
-// tcgen05 (TMEM allocation, loads/stores, MMA, commit) and cluster shared
-// memory. Every wait is bounded: after the limit it raises a device flag and
+// tcgen05 (TMEM allocation, loads, MMA, commit), programmatic dependent
+// launch and L2-level exchange between CTAs. Every wait is bounded: after the limit it raises a device flag and
 // returns false so the kernel can drain and exit instead of hanging.
 #pragma once
 #include <cuda.h>
@@ -69,6 +69,32 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream begin
+// launching, and wait until every kernel this one depends on has completed
+// and its memory is visible (a no-op when launched without the attribute).
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_prerequisites() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Global FP32 x4 store / load that bypass L1 (partial tiles exchanged
+// between CTAs through L2).
+__device__ __forceinline__ void stg_cg_f4(float* p, float4 v) {
+    asm volatile("st.global.cg.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
 // Bounded wait until the global word at `p` (written by other CTAs with
 // release semantics) reaches `value`: acquire loads, two-second limit, then
 // sets g_device_flags bit 0 and returns false.
@@ -104,18 +130,6 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
-}
-// 16-byte asynchronous copy global -> shared through L1-bypassing loads
-// (both addresses 16-byte aligned). Completion is tracked per thread.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t policy) {
-    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst),
-                 "l"(src), "l"(policy)
-                 : "memory");
-}
-// Arrive on `bar` once all of this thread's earlier cp.async copies have
-// landed; the arrival counts toward the barrier's expected count.
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
@@ -220,19 +234,6 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 32 lanes x 32 consecutive 32-bit columns; thread i owns lane (taddr.lane + i).
-__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31, %32};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-        "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-        "r"(v[29]), "r"(v[30]), "r"(v[31])
-        : "memory");
-}
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -244,27 +245,8 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&v)
         : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (BF16 inputs, FP32 accumulate).
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (BF16 inputs, FP32 accumulate).
-__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// The same MMA issued by one elected lane of a converged warp: every lane
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (BF16 inputs, FP32
+// accumulate), issued by one elected lane of a converged warp: every lane
 // computes the (warp-uniform) descriptors, so they stay in uniform registers
 // and the issue needs no per-lane register transfers.
 __device__ __forceinline__ void mma_bf16_ss_elect(uint32_t d_tmem, uint64_t a_desc,
@@ -285,12 +267,6 @@ __device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
         "elect.sync _|e, 0xffffffff;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
         ::"r"(bar)
-        : "memory");
-}
-// Arrive on `bar` once all previously issued tcgen05 MMAs of this thread finish.
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
         : "memory");
 }
 
@@ -314,57 +290,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
            | (uint64_t(2) << 61);                                   // SWIZZLE_128B
 }
 
-// ----------------------------------------------------------------- cluster
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Programmatic dependent launch: let the next kernel in the stream begin
-// launching, and wait until every kernel this one depends on has completed
-// and its memory is visible (a no-op when launched without the attribute).
-__device__ __forceinline__ void launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void wait_prerequisites() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// Global FP32 x4 store / load that bypass L1 (partial tiles exchanged
-// between CTAs through L2).
-__device__ __forceinline__ void stg_cg_f4(float* p, float4 v) {
-    asm volatile("st.global.cg.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
-                 "f"(v.z), "f"(v.w)
-                 : "memory");
-}
-__device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
-    float4 v;
-    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p)
-                 : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile(
-        "barrier.cluster.arrive.release.aligned;\n\t"
-        "barrier.cluster.wait.acquire.aligned;" ::
-            : "memory");
-}
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
-    return v;
-}
 
 // ------------------------------------------------------------ shared memory
 __device__ __forceinline__ uint32_t lds32(uint32_t a) {

@@ -585,7 +585,6 @@ struct DeviceInfo {
     int sms = 0;
     int smem_optin = 0;
     bool gemm_attr = false;
-    int active_clusters[17] = {};  // by cluster size, at the GEMM's shared memory budget
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_devices[kMaxDevices];
