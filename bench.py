@@ -199,13 +199,22 @@ def run_ours(args, world: int, rank: int) -> dict | None:
             dist.all_reduce(y)
         return y
 
+    align = torch.zeros(1, device=dev)
+
+    def settle():
+        """Keep the GPU busy while the host enqueues the step (so the timed
+        region measures the device, not host launch latency); with several
+        ranks, end with a tiny all-reduce so every rank's timed region starts
+        together instead of absorbing the other ranks' enqueue skew."""
+        torch.cuda._sleep(8_000_000)
+        if world > 1:
+            dist.all_reduce(align)
+
     def timed_step(fn) -> float:
         """One step (every call once, back to back) between two events."""
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
-        # Keep the GPU busy while the host enqueues the step, so the timed
-        # region measures the device, not host launch latency.
-        torch.cuda._sleep(8_000_000)
+        settle()
         start.record(stream)
         for c in calls:
             fn(c)
@@ -216,7 +225,7 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     def per_call_pass(fn, per_call: dict) -> None:
         """Every call between its own pair of events (for the per-shape table)."""
         events = []
-        torch.cuda._sleep(8_000_000)
+        settle()
         for c in calls:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
@@ -325,7 +334,7 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         "config": {
             "workload": "llama3-8b linears qkv/o/gate_up/down x tokens {1,8,16,32,64,128}",
             "tokens": list(args.tokens),
-            "split_k": "in-kernel cluster partition (auto)",
+            "split_k": "persistent stream-K schedule, K ranges summed in-kernel (FP32)",
             "l2": "no flush: every call reads its own weight copy, ~1.9 GB packed per step "
                   "(inputs larger than the 126 MB L2); calls run back to back between one "
                   "pair of events per step",
