@@ -89,7 +89,7 @@ struct RowDecoder {
     uint32_t xp_lo, xp_hi;
     // Multipliers kept in registers so address and selector arithmetic runs
     // as IMAD on the FMA pipe instead of shifts on the integer ALU pipe.
-    uint32_t k2, k4, k8, k128, krank, khi;
+    uint32_t kone, k2, k4, k8, k128, krank, khi;
 
     // The warp decodes band `band_` of both tiles; lane = tau*16 + rt*8 + r.
     __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int band_,
@@ -107,6 +107,7 @@ struct RowDecoder {
             xp[c >> 2] |= (((e & 1u) << 7) | (e >> 1)) << (8 * (c & 3));
         }
         xp_lo = xp[0], xp_hi = xp[1];
+        kone = ptx::launder(1u);
         k2 = ptx::launder(2u);
         k4 = ptx::launder(4u);
         k8 = ptx::launder(8u);
@@ -160,17 +161,20 @@ struct RowDecoder {
         const uint32_t ex0 = k0 - own0, ex1 = k1 - own1;
         const uint32_t cb = min(uint32_t(max(med.x, 0)), cap_c);
         const uint32_t rbase = min(uint32_t(max(med.y, 0)), cap_r);
+        // off[j]: shared address of segment j's first payload byte (the
+        // additions run on the FMA pipe, which has room to spare).
         uint32_t off[8];
-        uint32_t run = cb;
+        uint32_t run = common + cb;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t ex = j < 4 ? ex0 : ex1, tot = j < 4 ? tot0 : tot1;
-            off[j] = run + __byte_perm(ex, 0, 0x4440 | (j & 3));
-            run += __byte_perm(tot, 0, 0x4440 | (j & 3));
+            off[j] = ptx::mad_lo(__byte_perm(ex, 0, 0x4440 | (j & 3)), kone, run);
+            run = ptx::mad_lo(__byte_perm(tot, 0, 0x4440 | (j & 3)), kone, run);
         }
         // Rare words: segment j's run starts at rbase + (elements before the
-        // row segment in the band) - (common elements before it).
-        const uint32_t rconst = rbase + cb + row_elems;
+        // row segment in the band) - (common elements before it); `common`
+        // cancels out of the difference.
+        const uint32_t rconst = rbase + common + cb + row_elems;
 #pragma unroll
         for (int h = 0; h < 4; ++h)
             rs.ro[h] = __byte_perm(rconst + 128u * (2 * h) - off[2 * h],
@@ -181,8 +185,10 @@ struct RowDecoder {
                              __byte_perm(ind[6], ind[7], 0x0040), 0x5410);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
+            // The funnel shift takes the byte offset inside the word from
+            // the address's low bits.
             const uint32_t co = off[j];
-            const uint32_t aw = common + (co & ~3u);
+            const uint32_t aw = co & ~3u;
             const uint32_t w0 = ptx::lds_s32(aw), w1 = ptx::lds_s32(aw + 4), w2 = ptx::lds_s32(aw + 8);
             const uint32_t sh = ptx::mad_lo(co, k8, 0);
             const uint32_t q0 = __funnelshift_r(w0, w1, sh);
@@ -223,8 +229,8 @@ struct RowDecoder {
         for (int c = 0; c < 8; ++c)
             ptx::sts128(row + ((uint32_t(c) << 4) ^ swz),
                         make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]));
-        uint32_t rlo = all_common ? 0u : ~rs.i03, rhi = all_common ? 0u : ~rs.i47;
         const uint32_t rcap = cap_r ? cap_r - 1 : 0;
+        uint32_t rlo = all_common ? 0u : ~rs.i03, rhi = all_common ? 0u : ~rs.i47;
         // Rares are visited in row order; `run` counts the rares already
         // patched in the current segment, so the word of the rare at (j, c)
         // is ro_j + run.
@@ -243,7 +249,7 @@ struct RowDecoder {
             const uint32_t ro = __byte_perm(hi ? rs.ro[2] : rs.ro[0], hi ? rs.ro[3] : rs.ro[1],
                                             (j & 3u) * 0x22u + 0x10u);
             const uint32_t idx = min((ro + run) & 0xFFFFu, rcap);
-            const uint32_t word = ptx::lds_u16(rare + 2u * idx);
+            const uint32_t word = ptx::lds_u16(ptx::mad_lo(idx, k2, rare));
             // Element c of segment j: byte 2c of 16-byte chunk j, swizzled.
             ptx::sts16(row + (((2u * p) & 0x7Eu) ^ swz), word);
         }

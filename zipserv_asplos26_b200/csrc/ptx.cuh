@@ -52,19 +52,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// Wait for the phase with the given parity to complete. Gives up after about
-// two seconds (or 2^30 polls), sets g_device_flags bit 0 and returns false.
+// Same test, but a thread whose phase is not complete yet is suspended until
+// it completes or about `hint_ns` pass, instead of returning at once: waiting
+// warps then stop taking issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
+// Wait for the phase with the given parity to complete, suspended between
+// tests. Gives up after about two seconds, sets g_device_flags bit 0 and
+// returns false.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t start = 0;
-    for (uint32_t i = 1; i < (1u << 30); ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 0) {
-            const uint64_t now = global_timer_ns();
-            if (!start) start = now;
-            else if (now - start > 2000000000ull) break;
-        }
-    }
+    const uint64_t start = global_timer_ns();
+    do {
+        if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
+    } while (global_timer_ns() - start < 2000000000ull);
     atomicOr(&g_device_flags, 1u);
     return false;
 }
@@ -258,6 +270,44 @@ __device__ __forceinline__ void mma_bf16_ss_elect(uint32_t d_tmem, uint64_t a_de
         "elect.sync _|e, 0xffffffff;\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// One K slice of 64: four K = 16 MMAs (the first overwrites the accumulator
+// unless `accumulate`) and a commit to `bar`, all from one elected lane of a
+// converged warp. Descriptors are passed as their 32-bit halves: stepping
+// 16 K elements (32 bytes) adds 2 to the low half's start-address field,
+// which never carries out of it for shared-memory addresses.
+__device__ __forceinline__ void mma_bf16_slice_elect(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                                     uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
+                                                     uint32_t accumulate, uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, q;\n\t"
+        ".reg .b32 al, bl;\n\t"
+        ".reg .b64 ad, bd;\n\t"
+        "setp.ne.b32 p, %7, 0;\n\t"
+        "setp.eq.b32 q, %7, %7;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "mov.b64 ad, {%1, %2};\n\t"
+        "mov.b64 bd, {%3, %4};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t"
+        "add.u32 al, %1, 2;\n\t"
+        "add.u32 bl, %3, 2;\n\t"
+        "mov.b64 ad, {al, %2};\n\t"
+        "mov.b64 bd, {bl, %4};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
+        "add.u32 al, %1, 4;\n\t"
+        "add.u32 bl, %3, 4;\n\t"
+        "mov.b64 ad, {al, %2};\n\t"
+        "mov.b64 bd, {bl, %4};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
+        "add.u32 al, %1, 6;\n\t"
+        "add.u32 bl, %3, 6;\n\t"
+        "mov.b64 ad, {al, %2};\n\t"
+        "mov.b64 bd, {bl, %4};\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(
+            d_tmem),
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(bar), "r"(accumulate)
         : "memory");
 }
 // Commit from one elected lane of a converged warp (see mma_bf16_ss_elect).

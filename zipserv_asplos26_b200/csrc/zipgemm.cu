@@ -101,8 +101,8 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     const uint32_t sbase = ptx::smem_addr(smem);
     const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
     const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
-    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [abuf*NDG] A tile written
-    const uint32_t bar_aempty = bar_afull + 8 * kMaxATiles;  // [abuf*NDG] A tile read by MMAs
+    const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [na] A tile written
+    const uint32_t bar_aempty = bar_afull + 8 * kMaxATiles;  // [na] A tile read by MMAs
     const uint32_t bar_xfull = bar_aempty + 8 * kMaxATiles;   // [kMaxX]
     const uint32_t bar_xempty = bar_xfull + 8 * kMaxX;
     const uint32_t bar_d = bar_xempty + 8 * kMaxX;             // [2] accumulator complete
@@ -133,9 +133,13 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             ptx::mbar_init(bar_addr(bar_xfull, i), 1);
             ptx::mbar_init(bar_addr(bar_xempty, i), 1);
         }
+        // With one x slot per A tile, x slot i lands on A tile i's barrier
+        // (the x loader's arrival plus its bytes), so each step's MMAs wait
+        // on one barrier.
+        const uint32_t afull_count = p.nx == p.na ? 5u : 4u;
         for (int i = 0; i < kMaxATiles; ++i) {
-            ptx::mbar_init(bar_addr(bar_afull, i), 4);   // the group's four warps
-            ptx::mbar_init(bar_addr(bar_aempty, i), 1);  // MMA commit
+            ptx::mbar_init(bar_addr(bar_afull, i), afull_count);  // the group's four warps (+ x)
+            ptx::mbar_init(bar_addr(bar_aempty, i), 1);           // MMA commit
         }
         for (int b = 0; b < 2; ++b) {
             ptx::mbar_init(bar_addr(bar_d, b), 1);
@@ -163,43 +167,44 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
 
     if (warp == 0) {
         // ------------------------------------------------------ MMA issuer
-        // Step t: A = group t % NDG's tile a = t % (abuf * NDG), B = x slot
-        // t % nx (with nx == abuf * NDG the same index: one commit frees
-        // both). Segment s accumulates into TMEM buffer s & 1; its first MMA
-        // overwrites, and it waits until the epilogue of segment s - 2 has
-        // drained that buffer. The whole warp runs the loop in uniform
-        // control flow; one elected lane issues each MMA and commit.
+        // Step t: A tile a = t % na (written by group t % NDG), B = x slot
+        // t % nx (with nx == na the same index: one barrier says both
+        // landed and one commit frees both). Segment s accumulates into TMEM
+        // buffer s & 1; its first MMA overwrites, and it waits until the
+        // epilogue of segment s - 2 has drained that buffer. The whole warp
+        // runs the loop in uniform control flow; one elected lane issues
+        // each step's four MMAs and commit. This warp paces the CTA, so the
+        // loop is kept short: descriptors advance as 32-bit halves (the
+        // start-address field holds address >> 4, a tile of B bytes adds
+        // B >> 4) and common steps take a single barrier wait.
         const uint32_t idesc = ptx::idesc_bf16_m128(uint32_t(p.bn));
-        const int nx = p.nx, na = p.abuf * NDG;
+        const int nx = p.nx, na = p.na;
         const bool xmerged = nx == na;
-        // Descriptors advance by whole tiles: the start-address field holds
-        // address >> 4, so a tile of B bytes is B >> 4 in the descriptor.
         const uint64_t xdesc0 = ptx::smem_desc_sw128(sbase + p.off_x);
         const uint64_t adesc0 = ptx::smem_desc_sw128(sbase + p.off_a);
+        const uint32_t x_lo0 = uint32_t(xdesc0), x_hi = uint32_t(xdesc0 >> 32);
+        const uint32_t a_lo0 = uint32_t(adesc0), a_hi = uint32_t(adesc0 >> 32);
         const uint32_t xstep = p.x_bytes >> 4, astep = kATileBytes >> 4;
+        const uint32_t tcols = p.tmem_cols;
         int xs = 0, a = 0, s = 0, k = t_begin - unit0 * kt;
-        uint32_t xph = 0, aph = 0;
-        bool ok = true;
-        for (int t = 0; ok && t < nsteps; ++t) {
+        uint32_t xph = 0, aph = 0, x_lo = x_lo0, a_lo = a_lo0;
+        for (int t = 0; t < nsteps; ++t) {
             const bool first = t == 0 || k == 0, last = t == nsteps - 1 || k == kt - 1;
+            bool ok = true;
             if (first && s >= 2)
                 ok = ptx::mbar_wait(bar_addr(bar_tempty, s & 1), uint32_t((s >> 1) - 1) & 1u);
-            ok = ok && ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) &&
-                 ptx::mbar_wait(bar_addr(bar_afull, a), aph);
+            if (!xmerged) ok = ptx::mbar_wait(bar_addr(bar_xfull, xs), xph) && ok;
+            ok = ptx::mbar_wait(bar_addr(bar_afull, a), aph) && ok;
             if (!__all_sync(kFullMask, ok)) break;
             ptx::tc_fence_after();
-            const uint32_t d = tmem + uint32_t(s & 1) * p.tmem_cols;
-            const uint64_t bdesc = xdesc0 + uint32_t(xs) * xstep;
-            const uint64_t adesc = adesc0 + uint32_t(a) * astep;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                ptx::mma_bf16_ss_elect(d, adesc + 2u * kk, bdesc + 2u * kk, idesc,
-                                       !(first && kk == 0));
-            ptx::mma_commit_elect(bar_addr(bar_aempty, a));
+            ptx::mma_bf16_slice_elect(tmem + uint32_t(s & 1) * tcols, a_lo, a_hi, x_lo, x_hi, idesc,
+                                      first ? 0u : 1u, bar_addr(bar_aempty, a));
             if (!xmerged) ptx::mma_commit_elect(bar_addr(bar_xempty, xs));
             if (last) ptx::mma_commit_elect(bar_addr(bar_d, s & 1));  // segment complete
-            if (++xs == nx) xs = 0, xph ^= 1u;
-            if (++a == na) a = 0, aph ^= 1u;
+            if (++xs == nx) xs = 0, xph ^= 1u, x_lo = x_lo0;
+            else x_lo += xstep;
+            if (++a == na) a = 0, aph ^= 1u, a_lo = a_lo0;
+            else a_lo += astep;
             if (++k == kt) k = 0;
             if (last) ++s;
         }
@@ -213,15 +218,19 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             ptx::wait_prerequisites();
             const uint64_t pol_x = ptx::policy_evict_last();
             const int nx = p.nx;
-            const uint32_t freed = nx == p.abuf * NDG ? bar_aempty : bar_xempty;
+            // One x slot per A tile: x lands on the A tile's barrier and the
+            // A tile's commit frees it.
+            const bool xmerged = nx == p.na;
+            const uint32_t freed = xmerged ? bar_aempty : bar_xempty;
+            const uint32_t landed = xmerged ? bar_afull : bar_xfull;
             int issued = 0, k = t_begin - unit0 * kt, xs = 0;
             int ntok = (unit0 / rbs) * p.bn, rb = unit0 % rbs;  // token offset of the unit
             uint32_t fph = 0;  // parity of the `freed` completion awaited next
             for (int t = 0; t < nsteps; ++t) {
                 if (t >= nx && !ptx::mbar_wait(bar_addr(freed, xs), fph)) break;
-                ptx::mbar_arrive_expect_tx(bar_addr(bar_xfull, xs), p.x_bytes);
+                ptx::mbar_arrive_expect_tx(bar_addr(landed, xs), p.x_bytes);
                 ptx::tma_load_3d(sbase + p.off_x + uint32_t(xs) * p.x_bytes, &xmap, 0, ntok, k,
-                                 bar_addr(bar_xfull, xs), pol_x);
+                                 bar_addr(landed, xs), pol_x);
                 issued = t + 1;
                 if (++xs == nx) {
                     xs = 0;
@@ -234,7 +243,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             }
             // Never leave copies in flight: wait for the last loads to land.
             for (int t = max(0, issued - nx); t < issued; ++t)
-                ptx::mbar_wait(bar_addr(bar_xfull, t % nx), (t / nx) & 1);
+                ptx::mbar_wait(bar_addr(landed, t % nx), (t / nx) & 1);
         }
         __syncwarp();
     } else if (warp < 4) {
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         const uint32_t mr = uint32_t(32 * q + lane);
         const uint32_t arow = sbase + p.off_a + (mr >> 3) * 1024u + (mr & 7u) * 128u;
         const uint32_t swz = (mr & 7u) << 4;
-        const int na = p.abuf * NDG;
+        const int na = p.na;  // >= NDG
         bool ok = ptx::mbar_wait(bar_tab, 0);
 
         // Position of the group's step t, advanced without divisions.
@@ -370,9 +379,9 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
                        slot + L.med + uint32_t(tau) * 32u, slot + (tau ? L.common1 : L.common0),
                        cap_c, cap_r, out, rs);
-            if (!valid) {
+            if (__any_sync(kFullMask, !valid)) {  // only in a ragged last row block
 #pragma unroll
-                for (int w = 0; w < 32; ++w) out[w] = 0;
+                for (int w = 0; w < 32; ++w) out[w] = valid ? out[w] : 0u;
             }
             // A tile a = t % na is free once the MMAs of step t - na finished.
             if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
@@ -613,22 +622,22 @@ struct GemmLayout {
     int nx;
 };
 
-// Shared memory: barriers | lookup tables | A tiles (abuf 16 KB 128 x 64
-// BF16 tiles per decoder group, 1024-aligned) | x ring (nx slots of bn*128
+// Shared memory: barriers | lookup tables | A tiles (na 16 KB 128 x 64
+// BF16 tiles, 1024-aligned) | x ring (nx slots of bn*128
 // bytes) | compressed slots (two per group) | pad. The x ring gets one slot
 // per A tile when they fit (then an x slot is freed by the same commit as
 // its A tile), else as many as fit.
-GemmLayout gemm_layout(int ndg, int abuf, int bn, uint32_t plane_pitch, uint32_t cap_c,
+GemmLayout gemm_layout(int ndg, int na, int bn, uint32_t plane_pitch, uint32_t cap_c,
                        uint32_t cap_r, int smem_limit) {
     GemmLayout l{};
     l.off_a = round_up(kBarrierBytes + kTableBytes, 1024);
-    l.off_x = l.off_a + uint32_t(ndg * abuf) * kATileBytes;
+    l.off_x = l.off_a + uint32_t(na) * kATileBytes;
     l.x_bytes = uint32_t(bn) * 128;
     l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r);
     const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
     const uint32_t used = l.off_x + slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    l.nx = std::min<int>({kMaxX, ndg * abuf, int(avail / l.x_bytes)});
+    l.nx = std::min<int>({kMaxX, na, int(avail / l.x_bytes)});
     l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
     l.total = l.off_slots + slots + kRingPadBytes;
     return l;
@@ -931,16 +940,16 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     // the previous slice's MMAs), then fewer groups with double-buffered A
     // tiles. The x ring needs at least two slots.
     struct Choice {
-        int ndg, abuf;
+        int ndg, na;
     };
-    constexpr Choice kChoices[] = {{4, 1}, {3, 2}, {2, 2}, {2, 1}};
+    constexpr Choice kChoices[] = {{4, 4}, {3, 6}, {2, 4}, {2, 2}};
     int ndg = 0;
     GemmLayout l{};
     for (const Choice& c : kChoices) {
-        l = gemm_layout(c.ndg, c.abuf, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
+        l = gemm_layout(c.ndg, c.na, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
         if (l.nx >= 2) {
             ndg = c.ndg;
-            p.abuf = c.abuf;
+            p.na = c.na;
             break;
         }
     }

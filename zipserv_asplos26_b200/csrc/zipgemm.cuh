@@ -51,7 +51,8 @@ struct GemmParams {
                            // part's CTA may wait for a unit's other parts
     int bn;                // N tile (multiple of 16, <= 256)
     int nx;                // x ring slots
-    int abuf;              // decoded A tiles per decoder group (1 or 2)
+    int na;                // decoded A tiles (>= decoder groups, <= kMaxATiles); step t
+                           // writes tile t % na
     uint32_t cap_c, cap_r;  // payload capacity per tile (bytes, words)
     uint32_t start_exp;
     uint32_t plane_box_bytes;  // bytes one bitmap tensor load (or three) writes
