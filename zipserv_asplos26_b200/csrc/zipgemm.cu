@@ -124,45 +124,56 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     // The next kernel in the stream may start launching now; it waits for
     // this grid's completion before it reads anything this grid writes.
     ptx::launch_dependents();
-    if (tid == 0) {
-        for (int s = 0; s < 2 * NDG; ++s) {
-            ptx::mbar_init(bar_addr(bar_full, s), 1);
-            ptx::mbar_init(bar_addr(bar_free, s), 4);
+    // Prologue, overlapped across warps: warp 0 allocates TMEM while warp 1
+    // initialises the barriers (one lane per barrier) and starts the table
+    // copy, and the producers fetch their first step's offsets.
+    int2 first_offs = make_int2(0, 0);
+    if (warp == 0) {
+        ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 2 * p.tmem_cols);
+        ptx::tmem_relinquish();
+    } else if (warp == 1) {
+        if (lane < 2 * NDG) {
+            ptx::mbar_init(bar_addr(bar_full, lane), 1);
+            ptx::mbar_init(bar_addr(bar_free, lane), 4);
         }
-        for (int i = 0; i < kMaxX; ++i) {
-            ptx::mbar_init(bar_addr(bar_xfull, i), 1);
-            ptx::mbar_init(bar_addr(bar_xempty, i), 1);
+        if (lane < kMaxX) {
+            ptx::mbar_init(bar_addr(bar_xfull, lane), 1);
+            ptx::mbar_init(bar_addr(bar_xempty, lane), 1);
         }
         // With one x slot per A tile, x slot i lands on A tile i's barrier
         // (the x loader's arrival plus its bytes), so each step's MMAs wait
         // on one barrier.
-        const uint32_t afull_count = p.nx == p.na ? 5u : 4u;
-        for (int i = 0; i < kMaxATiles; ++i) {
-            ptx::mbar_init(bar_addr(bar_afull, i), afull_count);  // the group's four warps (+ x)
-            ptx::mbar_init(bar_addr(bar_aempty, i), 1);           // MMA commit
+        if (lane < kMaxATiles) {
+            ptx::mbar_init(bar_addr(bar_afull, lane), p.nx == p.na ? 5u : 4u);  // group (+ x)
+            ptx::mbar_init(bar_addr(bar_aempty, lane), 1);                       // MMA commit
         }
-        for (int b = 0; b < 2; ++b) {
-            ptx::mbar_init(bar_addr(bar_d, b), 1);
-            ptx::mbar_init(bar_addr(bar_tempty, b), 4);  // the epilogue warps
+        if (lane < 2) {
+            ptx::mbar_init(bar_addr(bar_d, lane), 1);
+            ptx::mbar_init(bar_addr(bar_tempty, lane), 4);  // the epilogue warps
         }
-        ptx::mbar_init(bar_tab, 1);
+        if (lane == 0) ptx::mbar_init(bar_tab, 1);
         ptx::fence_mbar_init();
-    }
-    if (warp == 0) {
-        ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 2 * p.tmem_cols);
-        ptx::tmem_relinquish();
+        if (lane == 0) {
+            ptx::prefetch_tensormap(&xmap);
+            ptx::prefetch_tensormap(&mmap);
+            for (int i = 0; i < pm.count; ++i) ptx::prefetch_tensormap(&pm.map[i]);
+            // Decode lookup tables: one bulk copy from the library's constant table.
+            ptx::mbar_arrive_expect_tx(bar_tab, kTableBytes);
+            ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
+        }
+    } else if (warp < 4 && lane < 4) {
+        // Producer pi's first step is pi: lane 2*r + e holds offset entry e of
+        // tile row r of its block.
+        const int pi = warp - 2;
+        int k = t_begin - unit0 * kt + pi, rb = unit0 % rbs;
+        if (k >= kt) k -= kt, rb = rb + 1 == rbs ? 0 : rb + 1;
+        const int tr = 2 * rb + (lane >> 1);
+        if (pi < nsteps && tr < p.row_tiles)
+            first_offs = reinterpret_cast<const int2*>(p.global)[size_t(tr) * kt + k + (lane & 1)];
     }
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
-    if (tid == 0) {
-        ptx::prefetch_tensormap(&xmap);
-        ptx::prefetch_tensormap(&mmap);
-        for (int i = 0; i < pm.count; ++i) ptx::prefetch_tensormap(&pm.map[i]);
-        // Decode lookup tables: one bulk copy from the library's constant table.
-        ptx::mbar_arrive_expect_tx(bar_tab, kTableBytes);
-        ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
-    }
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         advance(cur, pi);
         Pos nxt = cur;
         advance(nxt, 2);
-        int2 o = load_offsets(pi, cur);
+        int2 o = first_offs;  // load_offsets(pi, cur), fetched before the CTA sync
         bool ok = true;
         int last = -1;  // last step issued
         for (int t = pi, u = pi / NDG, g = pi % NDG; t < nsteps; t += 2) {
@@ -461,30 +472,31 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                            512u +
                        size_t(lane) * 16u;
             };
-            // acc += partials first .. parts - 1 of piece c, two loads in
-            // flight per round trip, summed in K order.
+            // acc += partials first .. parts - 1 of piece c, summed in K
+            // order. Two partials (all 16 values of each) are loaded per
+            // round trip to L2.
             auto add_partials = [&](int c, int first, float (&acc)[16]) {
+                for (int pp = first; pp < parts; pp += 2) {
+                    const bool two = pp + 1 < parts;
+                    const float* s0 = partial(pp, c);
+                    const float* s1 = two ? partial(pp + 1, c) : s0;
+                    float4 x[4], y[4];
 #pragma unroll
-                for (int h = 0; h < 16; h += 8) {
-                    float4 a0 = make_float4(acc[h], acc[h + 1], acc[h + 2], acc[h + 3]);
-                    float4 a1 = make_float4(acc[h + 4], acc[h + 5], acc[h + 6], acc[h + 7]);
-                    for (int pp = first; pp < parts; pp += 2) {
-                        const float* s0 = partial(pp, c) + h;
-                        const float4 x0 = ptx::ldg_cg_f4(s0), x1 = ptx::ldg_cg_f4(s0 + 4);
-                        float4 y0 = make_float4(0.f, 0.f, 0.f, 0.f), y1 = y0;
-                        if (pp + 1 < parts) {
-                            const float* s1 = partial(pp + 1, c) + h;
-                            y0 = ptx::ldg_cg_f4(s1), y1 = ptx::ldg_cg_f4(s1 + 4);
-                        }
-                        a0.x += x0.x, a0.y += x0.y, a0.z += x0.z, a0.w += x0.w;
-                        a1.x += x1.x, a1.y += x1.y, a1.z += x1.z, a1.w += x1.w;
-                        if (pp + 1 < parts) {
-                            a0.x += y0.x, a0.y += y0.y, a0.z += y0.z, a0.w += y0.w;
-                            a1.x += y1.x, a1.y += y1.y, a1.z += y1.z, a1.w += y1.w;
+                    for (int i = 0; i < 4; ++i) x[i] = ptx::ldg_cg_f4(s0 + 4 * i);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) y[i] = ptx::ldg_cg_f4(s1 + 4 * i);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        acc[4 * i] += x[i].x, acc[4 * i + 1] += x[i].y;
+                        acc[4 * i + 2] += x[i].z, acc[4 * i + 3] += x[i].w;
+                    }
+                    if (two) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            acc[4 * i] += y[i].x, acc[4 * i + 1] += y[i].y;
+                            acc[4 * i + 2] += y[i].z, acc[4 * i + 3] += y[i].w;
                         }
                     }
-                    acc[h] = a0.x, acc[h + 1] = a0.y, acc[h + 2] = a0.z, acc[h + 3] = a0.w;
-                    acc[h + 4] = a1.x, acc[h + 5] = a1.y, acc[h + 6] = a1.z, acc[h + 7] = a1.w;
                 }
             };
             if (p.resident && cta == c0) {
