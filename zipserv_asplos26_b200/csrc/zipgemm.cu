@@ -542,15 +542,17 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                                        : make_float4(0.f, 0.f, 0.f, 0.f));
             }
             ptx::tc_fence_before();
+            // The warp barrier orders every lane's partial stores before
+            // lane 0's release below, which publishes them GPU-wide.
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));  // TMEM read
-            __threadfence();  // partials visible before the arrivals count
-            __syncwarp();
             if (p.resident) {
                 if (lane == 0)
                     ptx::red_release_add(p.ws_counters + size_t(unit) * 4u + size_t(q), 1u);
                 continue;
             }
+            __threadfence();  // each lane's partials visible before its arrival counts
+            __syncwarp();
             // Not every CTA resident: whoever delivers a piece's last partial
             // reduces it.
             uint32_t* counters = p.ws_counters + size_t(unit) * size_t(p.pieces) + piece0;
