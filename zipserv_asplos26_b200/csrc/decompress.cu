@@ -5,16 +5,21 @@
 // consecutive global tiles (row-major tile order) with stride gridDim.x; the
 // packed streams of a chunk are contiguous, so a chunk arrives with five
 // copies whatever its length. Warp roles:
-//   warp 0     producer: bulk async copies of each chunk's bitmaps, band
-//              offsets and payloads into a ring of shared-memory slots;
-//   warps 1..8 two decoder groups (four warps each, one chunk per group at
-//              a time); pair j of a chunk is tile j of each half, and warp w
-//              decodes 16-row band w%4 of both tiles of the pair, a thread
+//   warp 0, warps after the decoders
+//              producers (chunks rotate between them): bulk async copies
+//              of each chunk's bitmaps, band offsets and payloads into a
+//              ring of shared-memory slots;
+//   warps 1..16 four decoder groups (four warps each, one chunk per group
+//              at a time); pair j of a chunk is tile j of each half, and warp
+//              w decodes 16-row band w%4 of both tiles of the pair, a thread
 //              rebuilding one 64-element row with the shared row decoder.
 //              The warp writes its rows into a 32x64 staging tile in the
 //              128-byte-swizzled layout and one lane stores each 16-row half
-//              to HBM with a TMA tensor store (full 128-byte lines,
-//              double-buffered so decoding overlaps the store).
+//              to HBM with a TMA tensor store (full 128-byte lines); the next
+//              pair is decoded while the store drains and only its staging
+//              waits for the store to have read the tile.
+// Sixteen decoder warps (four per SM sub-partition) hide the decoder's
+// instruction latencies; fewer leave the issue slots half idle.
 // Reference kernel this replaces: csrc/L_Kernel.cuh:1147-1278 (one tile per
 // CTA, load -> sync -> decode -> sync -> 16-byte stores, no overlap).
 #include <cuda.h>
@@ -34,9 +39,10 @@
 
 namespace zs {
 
-constexpr int kDecGroups = 2;
-constexpr int kDecThreads = 32 + 128 * kDecGroups;
-constexpr int kDecStages = 8;  // ring slots at most; fewer when payload capacities are large
+constexpr int kDecGroups = 4;
+constexpr int kDecProducers = 3;
+constexpr int kDecThreads = 32 * kDecProducers + 128 * kDecGroups;
+constexpr int kDecStages = 12;  // ring slots at most; fewer when payload capacities are large
 constexpr uint32_t kOutTileBytes = 32 * 128;  // one warp's 32 rows x 64 BF16
 
 __global__ void __launch_bounds__(kDecThreads, 1)
@@ -71,11 +77,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
     }
 
-    if (warp == 0) {
-        // ------------------------------------------------------ producer
+    if (warp == 0 || warp > 4 * kDecGroups) {
+        // ------------------------------------------------------ producers
         // Per chunk: one tensor load for the bitmap planes (tiles past the end
         // arrive zero-filled), one bulk copy of the band offsets, one of each
         // half's common payload and one of the chunk's rare payload.
+        // This producer's chunks: pi, pi + kDecProducers, ...
+        const int pi = warp == 0 ? 0 : warp - 4 * kDecGroups;
         const uint64_t pol = ptx::policy_evict_first();
         const int2* goffs = reinterpret_cast<const int2*>(p.global);
         const uint32_t plane_bytes = 3u * 512u * uint32_t(C);
@@ -85,12 +93,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             const int t = (int(blockIdx.x) + it * int(gridDim.x)) * C + lane;
             return (it < nlocal && lane <= C) ? goffs[min(t, p.tiles)] : make_int2(0, 0);
         };
-        int2 next = load(0);
+        int2 next = load(pi);
         bool ok = true;
-        int issued = 0;
-        for (int it = 0; it < nlocal; ++it) {
+        int last = -1;  // last chunk issued
+        for (int it = pi; it < nlocal; it += kDecProducers) {
             const int2 cur = next;
-            next = load(it + 1);
+            next = load(it + kDecProducers);
             const int s = it % p.nstages;
             if (it >= p.nstages && lane == 0)
                 ok = ptx::mbar_wait(bar_empty + 8 * s, ((it / p.nstages) - 1) & 1);
@@ -140,10 +148,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (lane == 4 && clen0) ptx::bulk_g2s(slot + L.common0, p.sm + st[0].x, clen0, full, pol);
             if (lane == 5 && clen1) ptx::bulk_g2s(slot + L.common1, p.sm + st[1].x, clen1, full, pol);
             if (lane == 6 && rlen) ptx::bulk_g2s(slot + L.rare0, p.rare + st[0].y, rlen, full, pol);
-            ++issued;
+            last = it;
         }
+        // Never leave copies in flight: wait for this producer's chunks that
+        // are the last use of their slot (earlier uses were consumed before
+        // their slot was refilled; a later use, possibly another producer's,
+        // would advance the barrier past the awaited phase).
         if (lane == 0)
-            for (int it = max(0, issued - p.nstages); it < issued; ++it)
+            for (int it = last; it >= 0 && it >= nlocal - p.nstages; it -= kDecProducers)
                 ptx::mbar_wait(bar_full + 8 * (it % p.nstages), (it / p.nstages) & 1);
         __syncwarp();
     } else {
@@ -154,10 +166,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const int tau = lane >> 4;
         RowDecoder dec;
         dec.init(tables, lane, q, p.start_exp);
-        const uint32_t obuf = sbase + p.off_out + uint32_t(dw) * 2 * kOutTileBytes;
+        const uint32_t obuf = sbase + p.off_out + uint32_t(dw) * kOutTileBytes;
         uint32_t out[32];
         RareState rs;
-        int nstore = 0;
         bool ok = ptx::mbar_wait(bar_tab, 0);
         for (int it = g; it < nlocal; it += kDecGroups) {
             const int s = it % p.nstages;
@@ -177,8 +188,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 // position c ^ (row & 7) (the TMA 128-byte swizzle); rare
                 // elements are patched in place. A missing second tile is
                 // staged but never stored.
-                const uint32_t buf = obuf + uint32_t(nstore & 1) * kOutTileBytes;
-                if (lane == 0) ptx::bulk_wait_read<1>();
+                const uint32_t buf = obuf;
+                if (lane == 0) ptx::bulk_wait_read<0>();  // previous pair's store has read it
                 __syncwarp();
                 dec.store(buf + uint32_t(lane) * 128u, uint32_t(lane & 7) << 4, out, rs,
                           slot + L.rare0 + 2u * uint32_t(hdr.y), cap_r, tau == 1 && j >= n1);
@@ -192,7 +203,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                                           buf + 16 * 128);
                     ptx::bulk_commit();
                 }
-                ++nstore;
             }
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
@@ -228,17 +238,17 @@ cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* r
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
     p.off_out = round_up_u(kBarrierBytes + kTableBytes, 1024);
-    p.off_slots = p.off_out + 4 * kDecGroups * 2 * kOutTileBytes;
+    p.off_slots = p.off_out + 4 * kDecGroups * kOutTileBytes;
     const uint32_t used = p.off_slots + kRingPadBytes;
     const uint32_t avail = uint32_t(smem_optin) > used ? uint32_t(smem_optin) - used : 0;
-    // Largest half (tiles per copy run) that still leaves four slots, else
-    // two; the slot count is a multiple of the group count so each group
-    // owns the slots it consumes.
+    // Largest half (tiles per copy run) that still leaves two slots per
+    // decoder group (one being decoded, one landing), else fewer. Chunk i
+    // uses slot i % nstages whatever group decodes it.
     p.nstages = 0;
-    for (int min_slots : {4, 2}) {
+    for (int min_slots : {2 * kDecGroups, kDecGroups + 2, 2}) {
         for (int half : {4, 2, 1}) {
             const SlotLayout l = decompress_slot_layout(half, p.cap_c, p.cap_r);
-            const int n = std::min<int>(kDecStages, int(avail / l.bytes)) / kDecGroups * kDecGroups;
+            const int n = std::min<int>(kDecStages, int(avail / l.bytes));
             if (n >= min_slots) {
                 p.half = half, p.slot = l, p.nstages = n;
                 break;
