@@ -63,3 +63,15 @@ def test_decode_into_strided_destination_rejected_and_aligned_ok(native_lib, ora
                               packed.start_exp, base.data_ptr() + 16, 128, 128) == 0
     torch.cuda.synchronize()
     assert np.array_equal(words_of(base[8:]).reshape(128, 128), words)
+
+
+@pytest.mark.parametrize("m,k,outliers", [(64, 64, 0.0), (128, 6400, 0.0), (2368, 1024, 0.0),
+                                          (9472, 384, 0.02), (4160, 2112, 0.1)])
+def test_chunk_schedules(native_lib, oracle_mod, m, k, outliers):
+    """Chunk counts below, at and a few times the persistent grid (one chunk,
+    fewer chunks than CTAs, 2-3 chunks per CTA, uneven tails), with payload
+    capacities that change the slot ring: every producer drains its last
+    copies and no bounded wait gives up."""
+    words = oracle_mod.llama_weight(m, k, seed=5, outliers=outliers)
+    packed = runtime.compress(bf16_tensor(words))
+    assert np.array_equal(decode_gpu(packed), words)
