@@ -119,6 +119,22 @@ int zipserv_mm_ws(void* stream, const void* sm, const void* rare, const void* b1
                   int n, int k, int k_parts, void* partials, uint64_t partial_bytes,
                   void* counters, uint64_t counter_bytes);
 
+/* No counterpart in the reference. zipserv_mm_kparts for callers that cannot
+ * allocate device memory (bindings that hold only the buffers handed to them,
+ * engines whose memory budget is fully committed at start-up): its K-range
+ * scratch is a fixed 16 MiB array in the library's device memory, present on
+ * every GPU that loads the library until the process exits, so the call
+ * allocates nothing. Shapes needing more scratch than it holds return
+ * cudaErrorInvalidValue with the sizes in zipserv_error() (the default
+ * schedule fits up to 96 tokens on a 148-SM B200). The first call on a device
+ * looks up the array's device address; make it before any stream capture.
+ * Every call shares the one array: calls that can overlap on the GPU (other
+ * streams, other threads) race and must be ordered by the caller. */
+int zipserv_mm_noalloc(void* stream, const void* sm, const void* rare, const void* b1,
+                       const void* b2, const void* b3, const void* medium, const void* global,
+                       int max_common, int max_rare, int start_exp, const void* x, void* y,
+                       int m, int n, int k, int k_parts);
+
 /* The K partition zipserv_mm picks for this shape on the current device, or
  * a negative value if the shape is invalid. */
 int zipserv_mm_plan(int m, int n, int k);

@@ -3,3 +3,4 @@
 #include "zipgemm.cu"
 #include "decompress.cu"
 #include "capi_cuda.cu"
+#include "noalloc.cu"
