@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include <cstdio>
@@ -214,7 +215,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
 namespace {
 uint32_t round_up_u(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
-int g_dec_smem_set[64];
+std::atomic<int> g_dec_smem_set[64];  // shared-memory attribute set on a device
 }  // namespace
 
 cudaError_t launch_decompress(cudaStream_t stream, const void* sm, const void* rare,

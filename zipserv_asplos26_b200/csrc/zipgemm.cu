@@ -42,6 +42,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -604,10 +605,12 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// Filled once per device; `sms` is published last (release), so a thread
+// that reads it nonzero (acquire) also sees smem_optin.
 struct DeviceInfo {
-    int sms = 0;
+    std::atomic<int> sms{0};
     int smem_optin = 0;
-    bool gemm_attr = false;
+    std::atomic<bool> gemm_attr{false};
 };
 constexpr int kMaxDevices = 64;
 DeviceInfo g_devices[kMaxDevices];
@@ -615,14 +618,14 @@ std::mutex g_device_mutex;
 
 DeviceInfo& device_info(int device) {
     DeviceInfo& d = g_devices[device];
-    if (!d.sms) {
+    if (!d.sms.load(std::memory_order_acquire)) {
         std::lock_guard<std::mutex> lock(g_device_mutex);
-        if (!d.sms) {
+        if (!d.sms.load(std::memory_order_relaxed)) {
             int smem = 0, sms = 0;
             cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
             d.smem_optin = smem;
-            d.sms = sms;
+            d.sms.store(sms, std::memory_order_release);
         }
     }
     return d;
