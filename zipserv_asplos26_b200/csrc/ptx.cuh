@@ -81,6 +81,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
+// Named barrier `id` (1..15; 0 is __syncthreads) over `threads` threads,
+// whole warps.
+__device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // Programmatic dependent launch: let the next kernel in the stream begin
 // launching, and wait until every kernel this one depends on has completed
 // and its memory is visible (a no-op when launched without the attribute).

@@ -87,6 +87,92 @@ __device__ __forceinline__ int step_owner(int item, const GemmParams& p) {
     return int((int64_t(item + 1) * p.grid - 1) / p.steps);
 }
 
+// One 16-column chunk of a resident reducer's row block: its own K part
+// from TMEM plus the other parts' published pieces, added in K order (two
+// whole pieces per L2 round trip), converted and stored. Run by the epilogue
+// warp of a TMEM lane quarter and, since the reducer's segment is its CTA's
+// last, by the idle decoder warps of the same quarter, each on its share of
+// the chunks. `tbase` is the quarter's lanes of the segment's accumulator.
+struct ChunkReduce {
+    float* ws_partials;
+    uint16_t* y;
+    int m, n, bn, pieces;
+    uint32_t tbase;
+    int c0, parts, nb, mrow, lane;
+    size_t piece0;  // the quarter's first piece
+    bool row_ok, dok, wok;
+
+    __device__ __forceinline__ void run(int c) const {
+        uint32_t v[16];
+        ptx::tmem_ld_32x32b_x16(tbase + 16u * uint32_t(c), v);
+        ptx::tmem_wait_ld();
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = dok ? __uint_as_float(v[j]) : 0.f;
+        // Part pp >= 1 is CTA c0 + pp's first segment (partial slot 0).
+        auto piece = [&](int pp) {
+            return ws_partials +
+                   ((size_t(c0 + pp) * 2) * size_t(pieces) + piece0 + size_t(c)) * 512u +
+                   size_t(lane) * 16u;
+        };
+        for (int pp = 1; wok && pp < parts; pp += 2) {
+            const bool two = pp + 1 < parts;
+            const float* s0 = piece(pp);
+            const float* s1 = two ? piece(pp + 1) : s0;
+            float4 x[4], y[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x[i] = ptx::ldg_cg_f4(s0 + 4 * i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) y[i] = ptx::ldg_cg_f4(s1 + 4 * i);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[4 * i] += x[i].x, acc[4 * i + 1] += x[i].y;
+                acc[4 * i + 2] += x[i].z, acc[4 * i + 3] += x[i].w;
+            }
+            if (two) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[4 * i] += y[i].x, acc[4 * i + 1] += y[i].y;
+                    acc[4 * i + 2] += y[i].z, acc[4 * i + 3] += y[i].w;
+                }
+            }
+        }
+        if (!row_ok) return;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int nn = nb * bn + 16 * c + j;
+            if (nn < n)
+                y[size_t(nn) * m + mrow] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[j]));
+        }
+    }
+};
+
+// A decoder warp's share of its CTA's last-segment reduction (kept out of
+// line so the decoder loop's register allocation is not affected).
+__device__ __noinline__ void help_reduce(float* ws_partials, uint16_t* y, uint32_t* ws_counters,
+                                         int m, int n, int bn, int pieces, uint32_t tmem_cols,
+                                         int grid, int steps, uint32_t tmem, uint32_t bar_d,
+                                         int unit, int s, int rbs, int kt, int cta, int g, int q,
+                                         int lane, int stride) {
+    const int b = s & 1, chunks = bn / 16, ubeg = unit * kt;
+    const bool dok = ptx::mbar_wait(bar_d + 8u * uint32_t(b), uint32_t(s >> 1) & 1u);
+    ptx::tc_fence_after();
+    ptx::wait_prerequisites();  // output writes, as in the epilogue
+    const int last_owner = int((int64_t(ubeg + kt - 1 + 1) * grid - 1) / steps);
+    const int parts = last_owner - cta + 1;
+    uint32_t* quarter = ws_counters + size_t(unit) * 4u + size_t(q);
+    bool wok = true;
+    if (lane == 0) wok = ptx::wait_global_geq(quarter, uint32_t(parts - 1));
+    wok = __shfl_sync(kFullMask, wok, 0);
+    const int mrow = (unit % rbs) * 128 + lane_row(32 * q + lane);
+    const ChunkReduce cr{ws_partials, y, m, n, bn, pieces,
+                         tmem + (uint32_t(32 * q) << 16) + uint32_t(b) * tmem_cols,
+                         cta, parts, unit / rbs, mrow, lane, size_t(q) * size_t(chunks),
+                         mrow < m, dok, wok};
+    for (int c = g + 1; c < chunks; c += stride) cr.run(c);
+    ptx::tc_fence_before();
+}
+
 // Warp roles: warp 0 allocates TMEM and issues the MMAs; warp 1 keeps the x
 // ring filled; warps 2-3 fill the decoder groups' compressed slots; warps
 // 4 .. 4 + 4*NDG - 1 form NDG decoder groups (local step t, item
@@ -413,6 +499,22 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 if (++rb == rbs) rb = 0;
             }
         }
+        // If the CTA's last segment is a row block it reduces (resident
+        // grids), help the epilogue warp of lane quarter q with it: group g
+        // takes chunks g + 1, g + 2 + NDG, ... . Every warp of the quarter
+        // meets at the quarter's named barrier, chunks or not.
+        if (p.resident && nseg > 0 && p.bn > 16) {
+            const int s = nseg - 1, unit = unit0 + s, ubeg = unit * kt;
+            const bool whole = t_begin <= ubeg && ubeg + kt <= t_end;
+            if (!whole && cta == step_owner(ubeg, p)) {
+                const int chunks = p.bn / 16;
+                if (g + 1 < chunks)
+                    help_reduce(p.ws_partials, p.y, p.ws_counters, p.m, p.n, p.bn, p.pieces,
+                                p.tmem_cols, p.grid, p.steps, tmem, bar_d, unit, s, rbs, kt, cta,
+                                g, q, lane, 1 + NDG);
+                ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
+            }
+        }
     } else {
         // ------------------------------------------------------ epilogue
         // Segment s (unit unit0 + s) is in accumulator s & 1. Whole units:
@@ -509,18 +611,17 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 bool wok = true;
                 if (lane == 0) wok = ptx::wait_global_geq(quarter, uint32_t(parts - 1));
                 wok = __shfl_sync(kFullMask, wok, 0);
-                for (int c = 0; c < chunks; ++c) {
-                    uint32_t v[16];
-                    ptx::tmem_ld_32x32b_x16(tbase + 16u * c, v);
-                    ptx::tmem_wait_ld();
-                    float acc[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) acc[j] = dok ? __uint_as_float(v[j]) : 0.f;
-                    if (wok) add_partials(c, 1, acc);
-                    if (row_ok) store_row(nb, c, mrow, acc);
-                }
+                // Chunks 0, 1 + NDG, ...; the quarter's decoder warps take the
+                // others (this is the CTA's last segment, so they are idle).
+                const ChunkReduce cr{p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, tbase, c0, parts,
+                                     nb, mrow, lane, piece0, row_ok, dok, wok};
+                // With one chunk (N tile 16) the epilogue warp works alone.
+                const int stride = chunks > 1 ? 1 + NDG : 1;
+                for (int c = 0; c < chunks; c += stride) cr.run(c);
                 ptx::tc_fence_before();
-                __syncwarp();
+                // Every warp of the quarter has read the counter before it is reset.
+                if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
+                else __syncwarp();
                 if (lane == 0) {
                     ptx::mbar_arrive(bar_addr(bar_tempty, b));
                     *reinterpret_cast<volatile uint32_t*>(quarter) = 0u;  // ready for reuse
