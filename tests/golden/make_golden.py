@@ -3,7 +3,7 @@
 Run in a container that has the reference sources (it builds oracle/_ref from
 them first):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH_TO_REFERENCE_CHECKOUT]
 
 Every digest here comes from the reference compiled from its sources:
 ``zipserv::pack_bf16`` (csrc/HostPacker.h), the frozen legacy encoder
