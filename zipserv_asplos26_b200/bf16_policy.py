@@ -30,6 +30,15 @@ MAX_CLUSTER = 16          # largest explicit K partition the native API accepts
 STARTUP_SLICES = 3.0      # per-CTA fixed cost, in K-slice units (B200 measurement)
 
 
+# Token count above which decode + stock GEMM beats the fused kernel on a
+# B200, measured for the Llama-3-8B linears (per-call device time summed over
+# qkv, o, gate_up and down, cold L2): the fused kernel wins at 128 tokens,
+# decode + GEMM at 192 and above; small-M layers (qkv, o) cross near 128,
+# gate_up near 320. Use it as large_batch_tokens when running eagerly or with
+# CUDA-graph capture sizes within it.
+B200_LARGE_BATCH_TOKENS = 176
+
+
 @dataclass(frozen=True)
 class DispatchSettings:
     """Dispatch knobs (reference ``DispatchSettings``): ``fixed`` uses the
@@ -37,6 +46,9 @@ class DispatchSettings:
     above ``large_batch_tokens`` to decode + stock GEMM."""
 
     mode: str = "fixed"
+    # The reference's default. On a B200, B200_LARGE_BATCH_TOKENS is faster
+    # (see there); it is not the default because planned dispatch with
+    # full-decode CUDA graphs needs every capture size within this threshold.
     large_batch_tokens: int = 768
     workspace_bytes: int = 64 * 2**20
     partial_dtype: str = "bf16"
