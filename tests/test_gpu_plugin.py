@@ -88,3 +88,25 @@ def test_fused_route_in_cuda_graph(fake):
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), eager.view(torch.int16))
+
+
+def test_padded_rows_forward(fake):
+    """pad_rows: a 1000-row layer is packed as 1024 rows (the pad repeats the
+    first rows); both routes return exactly the 1000 real output columns."""
+    settings = fake.plugin.DispatchSettings(mode="shape", large_batch_tokens=64)
+    method = fake.plugin.ZipServLinearMethod(1, settings, pad_rows=True)
+    layer, weight = _layer(fake, method, m=1000, k=512)
+    method.process_weights_after_loading(layer)
+    assert layer.zipserv_compressed and layer.zipserv_metadata[:2] == (1024, 512)
+    w = weight.cuda()
+    bias = torch.randn(1000, generator=torch.Generator().manual_seed(8)).to(torch.bfloat16).cuda()
+    g = torch.Generator().manual_seed(9)
+    small = torch.randn(16, 512, generator=g).to(torch.bfloat16).cuda()   # fused route
+    large = torch.randn(200, 512, generator=g).to(torch.bfloat16).cuda()  # decode + stock GEMM
+    y = method.apply(layer, small, bias)
+    torch.cuda.synchronize()
+    assert y.shape == (16, 1000) and y.is_contiguous()
+    mx, mean = rel_errors(words_of(y), words_of(_reference(small, w, bias)))
+    assert mx <= MAX_REL_TOL and mean <= MEAN_REL_TOL, (mx, mean)
+    assert torch.equal(method.apply(layer, large, bias).view(torch.int16),
+                       F.linear(large, w, bias).view(torch.int16))

@@ -252,3 +252,29 @@ def test_planned_dispatch_guards(fake):
     method.process_weights_after_loading(layer)
     assert layer.zipserv_compressed and layer.zipserv_sm_count == 148
     assert layer.zipserv_stock_gemm is not None
+
+
+def test_unaligned_rows_stay_dense_unless_padding_is_requested(fake, oracle_mod):
+    """An output size that is not a multiple of 64 keeps the stock weight by
+    default (the reference plugin's behaviour); with `pad_rows` it is packed
+    as the next multiple of 64 rows, the pad repeating the first rows."""
+    method = fake.plugin.ZipServLinearMethod()
+    layer, weight = _layer(fake, method, m=100, k=256)
+    method.process_weights_after_loading(layer)
+    assert not layer.zipserv_compressed and "64-aligned" in layer.zipserv_fallback_reason
+    assert torch.equal(layer.weight.data.view(torch.int16), weight.view(torch.int16))
+
+    cfg = fake.plugin.ZipServConfig.from_config({"pad_rows": True})
+    method = cfg.get_quant_method(fake.LinearBase(), "model.layers.0.o_proj")
+    assert method.pad_rows
+    layer, weight = _layer(fake, method, m=100, k=256)
+    method.process_weights_after_loading(layer)
+    assert layer.zipserv_compressed and layer.zipserv_rows == 100
+    m, k, _, _, start_exp = layer.zipserv_metadata
+    assert (m, k) == (128, 256)
+    from zipserv_asplos26_b200.runtime import BUFFER_NAMES
+    buffers = [getattr(layer, "zipserv_" + n).numpy() for n in BUFFER_NAMES]
+    padded = torch.cat((weight, weight[:28])).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(oracle_mod.decode(buffers, m, k, start_exp), padded)
+    with pytest.raises(ValueError):
+        fake.plugin.ZipServConfig.from_config({"pad_rows": "yes"})

@@ -53,11 +53,14 @@ class ZipServConfig(QuantizationConfig):
     """Online lossless packing of raw BF16 checkpoints (method "zipserv")."""
 
     def __init__(self, split_k: int = 1, ignore: tuple[str, ...] = (),
-                 dispatch: DispatchSettings = DEFAULT_DISPATCH) -> None:
+                 dispatch: DispatchSettings = DEFAULT_DISPATCH, pad_rows: bool = False) -> None:
         super().__init__()
         if type(split_k) is not int or split_k < 1:
             raise ValueError("split_k must be positive")
+        if type(pad_rows) is not bool:
+            raise ValueError("pad_rows must be true or false")
         self.split_k, self.ignore, self.dispatch = split_k, tuple(ignore), dispatch
+        self.pad_rows = pad_rows
 
     def get_name(self) -> str:
         return "zipserv"
@@ -85,7 +88,8 @@ class ZipServConfig(QuantizationConfig):
             raise ValueError("ignore must be a list of exact vLLM module prefixes")
         knobs = {key: config[key] for key in _DISPATCH_KEYS if key in config}
         dispatch = DispatchSettings(mode=config.get("dispatch", "fixed"), **knobs)
-        return cls(config.get("split_k", 1), tuple(ignore), dispatch)
+        return cls(config.get("split_k", 1), tuple(ignore), dispatch,
+                   config.get("pad_rows", False))
 
     def get_quant_method(self, layer: nn.Module, prefix: str) -> LinearMethodBase | None:
         """Compress dense linears; router gates and ignored prefixes stay stock."""
@@ -96,7 +100,7 @@ class ZipServConfig(QuantizationConfig):
         if isinstance(layer, GateLinear) or prefix in self.ignore:
             logger.info("ZipServ keeps stock linear dispatch for %s", prefix)
             return UnquantizedLinearMethod()
-        return ZipServLinearMethod(self.split_k, self.dispatch)
+        return ZipServLinearMethod(self.split_k, self.dispatch, self.pad_rows)
 
 
 def _target_device() -> torch.device:
@@ -117,8 +121,9 @@ class ZipServLinearMethod(LinearMethodBase):
 
     requires_device_loading = False
 
-    def __init__(self, split_k: int = 1, dispatch: DispatchSettings = DEFAULT_DISPATCH) -> None:
-        self.split_k, self.dispatch = split_k, dispatch
+    def __init__(self, split_k: int = 1, dispatch: DispatchSettings = DEFAULT_DISPATCH,
+                 pad_rows: bool = False) -> None:
+        self.split_k, self.dispatch, self.pad_rows = split_k, dispatch, pad_rows
 
     def create_weights(self, layer: nn.Module, input_size_per_partition: int,
                        output_partition_sizes: list[int], input_size: int, output_size: int,
@@ -153,8 +158,18 @@ class ZipServLinearMethod(LinearMethodBase):
         return max_tokens, compilation
 
     def process_weights_after_loading(self, layer: nn.Module) -> None:
-        weight = layer.weight.detach()
-        m, k = weight.shape
+        original = weight = layer.weight.detach()
+        rows, k = weight.shape
+        layer.zipserv_rows = rows
+        # With pad_rows, an output size that is not a multiple of 64 is packed
+        # with its first rows repeated up to the next multiple (repeating real
+        # rows keeps the pad's exponents inside the matrix's window, where
+        # zero rows could make a tile of exceptions that raises the payload
+        # capacity of every tile); outputs are cropped back to `rows`.
+        if self.pad_rows and rows > 0 and rows % 64:
+            extra = -rows % 64
+            weight = torch.cat((weight, weight[torch.arange(extra) % rows]), dim=0)
+        m = weight.shape[0]
         device = _target_device()
         max_tokens, compilation = self._planned_tokens()
         settings = self.dispatch
@@ -186,14 +201,14 @@ class ZipServLinearMethod(LinearMethodBase):
         if reason is not None:
             logger.warning("ZipServ keeps dense weight %s (max_planned_tokens=%s, Split-K=%s): %s",
                            (m, k), max_tokens, self.split_k, reason)
-            _keep_dense(layer, weight, device, reason)
+            _keep_dense(layer, original, device, reason)
             return
         if settings.partial_dtype == "fp32":
             require_fp32_partials()
         packed = compress(weight.cpu())
-        if packed.storage_bytes >= weight.numel() * weight.element_size():
-            logger.info("ZipServ keeps dense weight %s: packed weight does not shrink", (m, k))
-            _keep_dense(layer, weight, device, "Packed weight does not shrink")
+        if packed.storage_bytes >= original.numel() * original.element_size():
+            logger.info("ZipServ keeps dense weight %s: packed weight does not shrink", (rows, k))
+            _keep_dense(layer, original, device, "Packed weight does not shrink")
             return
         packed = packed.to(device)
         for name, buffer in zip(BUFFER_NAMES, packed.buffers, strict=True):
@@ -212,6 +227,7 @@ class ZipServLinearMethod(LinearMethodBase):
             return torch.nn.functional.linear(x, layer.weight, bias)
         buffers = [getattr(layer, "zipserv_" + name) for name in BUFFER_NAMES]
         m, k, *_ = layer.zipserv_metadata
+        rows = getattr(layer, "zipserv_rows", m)
         settings = self.dispatch
         split = (self.split_k if settings.mode == "fixed" else
                  select_split(m, x.numel() // k, k, layer.zipserv_sm_count, settings,
@@ -221,6 +237,8 @@ class ZipServLinearMethod(LinearMethodBase):
                 raise RuntimeError("The large-batch decode route is excluded from CUDA graphs")
             packed = PackedWeight(tuple(buffers), *layer.zipserv_metadata)
             dense = decompress(packed, max_bytes=settings.decode_workspace_bytes)
-            return layer.zipserv_stock_gemm(layer, x, dense, bias)
+            return layer.zipserv_stock_gemm(layer, x, dense[:rows], bias)
         y = _linear(x, buffers, *layer.zipserv_metadata, split, settings.partial_dtype == "fp32")
+        if rows != m:
+            y = y[..., :rows].contiguous()
         return y if bias is None else y + bias
