@@ -3,16 +3,19 @@ memory (bindings that only hold the buffers they are given, engines whose
 memory is fully committed at start-up): its K-range scratch is a fixed array
 in the library's device memory instead of a cudaMalloc'd buffer.
 
-Called through the C ABI, it must give the same results as zipserv_mm on the
-same inputs (within the parity tolerance), including on consecutive calls,
-which reuse the array the previous call left behind; shapes that need more
-scratch than the array holds are refused with a clear error. This file is
+Called through the C ABI, it must give exactly the words zipserv_mm gives on
+the same inputs (both run the same deterministic schedule and K-order
+reduction), within the parity tolerance of the CPU oracle's FP32 GEMM,
+including on consecutive calls, which reuse the array the previous call left
+behind; shapes that need more scratch than the array holds are refused with a
+clear error. This file is
 collected last, so a run that stops at the first failure has run every
 other test first."""
 from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
@@ -34,8 +37,13 @@ def lib(native_lib):
 
 
 @pytest.fixture(scope="module")
-def packed(native_lib, oracle_mod):
-    return runtime.compress(bf16_tensor(oracle_mod.llama_weight(M, K, seed=21))).to("cuda")
+def weight(oracle_mod):
+    return oracle_mod.llama_weight(M, K, seed=21)
+
+
+@pytest.fixture(scope="module")
+def packed(native_lib, weight):
+    return runtime.compress(bf16_tensor(weight)).to("cuda")
 
 
 def _args(packed):
@@ -58,19 +66,22 @@ def _mm(lib, packed, x, n):
     return rc, y
 
 
-def test_matches_zipserv_mm_on_consecutive_calls(lib, packed):
+def test_matches_zipserv_mm_on_consecutive_calls(lib, packed, weight, oracle_mod):
     g = torch.Generator().manual_seed(7)
     for n in (16, 64):  # two calls in a row; the second reuses the first's scratch
         partial, counters = runtime.workspace_size(M, n, K)
         assert partial > 0 and counters > 0  # the fixed scratch is really used
-        x = torch.randn(n, K, generator=g).to(torch.bfloat16).cuda()
-        rc, got = _noalloc(lib, packed, x, n)
+        x = torch.randn(n, K, generator=g).to(torch.bfloat16)
+        x_dev = x.cuda()
+        rc, got = _noalloc(lib, packed, x_dev, n)
         assert rc == 0, lib.zipserv_error()
-        rc, want = _mm(lib, packed, x, n)
+        rc, want = _mm(lib, packed, x_dev, n)
         assert rc == 0, lib.zipserv_error()
         torch.cuda.synchronize()
         assert runtime.device_flags() == 0
-        mx, mean = rel_errors(words_of(got), words_of(want))
+        assert np.array_equal(words_of(got), words_of(want)), n
+        expected, _ = oracle_mod.gemm(weight, words_of(x), threads=8)
+        mx, mean = rel_errors(words_of(got), expected)
         assert mx <= MAX_REL_TOL and mean <= MEAN_REL_TOL, (n, mx, mean)
 
 
