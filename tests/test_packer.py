@@ -35,7 +35,7 @@ def _sha_bytes(ptr: int, n: int) -> str:
 def compress(lib, words: np.ndarray):
     words = np.ascontiguousarray(words, dtype=np.uint16)
     m, k = words.shape
-    out = runtime._NativePacked()
+    out = runtime._Descriptor()
     status = lib.zipserv_compress(words.ctypes.data, m, k, ctypes.byref(out))
     return status, out
 
@@ -148,12 +148,12 @@ def test_init_api_rejects_bad_windows_and_tiles(init_api):
 def test_invalid_compress_inputs_leave_an_empty_descriptor(native_lib):
     w = np.zeros((64, 64), dtype=np.uint16)
     for m, k in ((0, 64), (64, 0), (-64, 64), (65, 64), (64, 96), (1 << 16, 1 << 16)):
-        out = runtime._NativePacked()
+        out = runtime._Descriptor()
         out.m = 99
         assert native_lib.zipserv_compress(w.ctypes.data, m, k, ctypes.byref(out)) == -1
         assert native_lib.zipserv_error()
         assert not any(out.buffers) and not any(out.lengths) and out.m == 0
-    out = runtime._NativePacked()
+    out = runtime._Descriptor()
     assert native_lib.zipserv_compress(None, 64, 64, ctypes.byref(out)) == -1
     assert native_lib.zipserv_compress(w.ctypes.data, 64, 64, None) == -1
     native_lib.zipserv_free(None)  # tolerated

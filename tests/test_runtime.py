@@ -1,8 +1,9 @@
 """Python runtime contracts on the CPU (reference tests/test_runtime.py:18-88
 and tests/test_host_runtime.py:22-238): input validation before the library
-loads, a missing library, storage accounting, zero-copy buffer sharing and
-ownership, fault injection around the native allocation (freed exactly
-once), the fake-tensor shape contract of the custom op, and decode budgets.
+loads, a missing library, storage accounting, the arena that holds a packed
+weight, fault injection around the native allocation (freed exactly once),
+the stored packed format, the fake-tensor shape contract of the custom op,
+and decode budgets.
 """
 from __future__ import annotations
 
@@ -78,64 +79,86 @@ def test_round_trip_and_to_cpu(native_lib, oracle_mod):
     assert np.array_equal(restored, w.view(torch.int16).numpy().view(np.uint16))
 
 
-def test_buffers_share_native_memory_until_the_last_view(native_lib, monkeypatch):
-    freed = []
-    original = runtime._free_packed
-
-    def counting_free(lib, native):
-        freed.append(tuple(native.buffers))
-        original(lib, native)
-
-    monkeypatch.setattr(runtime, "_free_packed", counting_free)
-    packed = runtime.compress(_weights())
-    keep = packed.buffers[2]
-    snapshot = keep.clone()
-    del packed
+def test_compress_returns_the_native_output_before_it_returns(native_lib, oracle_mod,
+                                                              monkeypatch):
+    """The encoder's native buffers are copied into the arena and freed at
+    once: the packed weight owns plain tensor memory (no finalizer ties it to
+    native allocations)."""
+    released = []
+    original = runtime._release
+    monkeypatch.setattr(runtime, "_release",
+                        lambda lib, d: (released.append(tuple(d.lengths)), original(lib, d)))
+    w = _weights(192, 256, seed=3)
+    packed = runtime.compress(w)
+    assert len(released) == 1
     gc.collect()
-    assert freed == []                     # one live view keeps the allocation
-    assert torch.equal(keep, snapshot)
-    del keep
-    gc.collect()
-    assert len(freed) == 1                 # released exactly once
+    bufs = [b.numpy() for b in packed.buffers]
+    restored = oracle_mod.decode(bufs, packed.m, packed.k, packed.start_exp)
+    assert np.array_equal(restored, w.view(torch.int16).numpy().view(np.uint16))
 
 
-def test_frombuffer_failure_frees_native_memory_once(native_lib, monkeypatch):
-    """tests/test_host_runtime.py:198-230: a failure while wrapping buffers
-    must release the native allocation exactly once."""
-    freed = []
-    original_free = runtime._free_packed
-    monkeypatch.setattr(runtime, "_free_packed",
-                        lambda lib, native: (freed.append(1), original_free(lib, native)))
-    calls = {"n": 0}
-    original = torch.frombuffer
+def test_copy_failure_frees_the_native_output_once(native_lib, monkeypatch):
+    """A failure while copying the encoder's output (here: the arena
+    allocation) still returns the native allocation, exactly once
+    (the reference's tests/test_host_runtime.py:198-230 asks the same of its
+    zero-copy wrapping)."""
+    released = []
+    original = runtime._release
+    monkeypatch.setattr(runtime, "_release",
+                        lambda lib, d: (released.append(1), original(lib, d)))
 
-    def flaky(*args, **kwargs):
-        calls["n"] += 1
-        if calls["n"] == 3:
-            raise MemoryError("simulated frombuffer failure")
-        return original(*args, **kwargs)
+    def failing_arena(*_a, **_k):
+        raise MemoryError("simulated arena allocation failure")
 
-    monkeypatch.setattr(torch, "frombuffer", flaky)
+    monkeypatch.setattr(runtime, "_new_arena", failing_arena)
     with pytest.raises(MemoryError):
         runtime.compress(_weights())
-    gc.collect()
-    assert len(freed) == 1
+    assert released == [1]
 
 
-def test_owner_allocation_failure_frees_native_memory(native_lib, monkeypatch):
-    calls = []
-    lib = runtime._library()
-    original = lib.zipserv_free
+def test_arena_layout(native_lib):
+    """Buffers are views of one arena at 256-byte aligned offsets, so the
+    three equally sized bitmap planes are equally spaced; moving to the same
+    device keeps the arena, and buffers made elsewhere are gathered."""
+    packed = runtime.compress(_weights(128, 256, seed=9))
+    base = packed.arena.data_ptr()
+    offsets = [b.data_ptr() - base for b in packed.buffers]
+    assert all(o % runtime.ARENA_ALIGN == 0 for o in offsets)
+    assert offsets[3] - offsets[2] == offsets[4] - offsets[3]
+    assert packed.to("cpu").arena is packed.arena
+    loose = runtime.PackedWeight(tuple(b.clone() for b in packed.buffers), packed.m, packed.k,
+                                 packed.max_common, packed.max_rare, packed.start_exp)
+    gathered = loose.to("cpu")
+    assert gathered.arena is not None and gathered.arena is not packed.arena
+    assert all(torch.equal(a, b) for a, b in zip(gathered.buffers, packed.buffers))
 
-    class FailingOwner:
-        def __init__(self, *_):
-            raise MemoryError("simulated owner allocation failure")
 
-    monkeypatch.setattr(runtime, "_NativeBufferOwner", FailingOwner)
-    monkeypatch.setattr(lib, "zipserv_free", lambda p: (calls.append(1), original(p)))
-    with pytest.raises(MemoryError):
-        runtime.compress(_weights())
-    assert len(calls) == 1
+def test_stored_format_round_trip_and_guards(native_lib, tmp_path):
+    packed = runtime.compress(_weights(128, 256, seed=11))
+    path = tmp_path / "w.zstb"
+    runtime.save_packed(packed, path)
+    back = runtime.load_packed(path)
+    assert (back.m, back.k, back.max_common, back.max_rare, back.start_exp) == (
+        packed.m, packed.k, packed.max_common, packed.max_rare, packed.start_exp)
+    assert all(torch.equal(a, b) for a, b in zip(back.buffers, packed.buffers))
+    data = path.read_bytes()
+    hdr = runtime._HEADER.size
+
+    def rejected(blob, match):
+        bad = tmp_path / "bad.zstb"
+        bad.write_bytes(blob)
+        with pytest.raises(ValueError, match=match):
+            runtime.load_packed(bad)
+
+    rejected(b"XXXXXXXX" + data[8:], "magic")
+    rejected(data[:8] + (2).to_bytes(4, "little") + data[12:], "version")
+    rejected(data[:hdr + 5] + bytes([data[hdr + 5] ^ 1]) + data[hdr + 6:], "checksum")
+    rejected(data[:-256], "truncated")
+    rejected(data[:10], "too short")
+    # A bitmap stream whose length does not match the shape.
+    fields = list(runtime._HEADER.unpack_from(data))
+    fields[9 + 2] += 8  # lengths start at field 9; bitmap1 is the third
+    rejected(runtime._HEADER.pack(*fields) + data[hdr:], "bitmap1")
 
 
 def test_native_validation_failure_raises_with_message(native_lib, monkeypatch):
