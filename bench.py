@@ -23,10 +23,16 @@ cuBLAS BF16 on the dense weights is timed the same way. With --gpus N
 (no collective), o/down by K with an NCCL all-reduce of the BF16 partial
 outputs inside the timed region.
 
---impl reference times the reference's CPU implementation of the path (the
-restated decoder and FP32 GEMM of oracle/, all host threads) on the same
-metric: each step decodes the o-projection weight and multiplies it with 8
-tokens.
+--impl reference times the reference's CPU implementation of the path on the
+same metric and config: each step runs all 24 calls of the sweep, each on a
+bounded sample of its weight (the first 256 rows, packed by the reference's
+own encoder built from its sources into oracle/_ref, then decoded and
+multiplied in FP32 by oracle/'s restatement of the reference's CPU decoder
+and GEMM, all host threads). The same sample, plus the encoder's own time,
+is the `cpu_baseline` of the default line. When oracle/_ref also holds the
+reference's CUDA bridge recompiled for sm_100a, the per-shape table gains
+`reference_gpu_us`: the reference's own fused kernel (mma.sync, its Split-K
+reduction kernel) on the same packed weights, best of split_k 1/2/4/8.
 """
 from __future__ import annotations
 
@@ -51,6 +57,41 @@ LAYERS = (  # name, M (out features), K (in features), tensor-parallel split
 )
 TOKENS = (1, 8, 16, 32, 64, 128)
 METRIC = "zipgemm_hbm_gbs_compressed_llama3_8b_decode_sweep"
+
+
+CPU_SAMPLE_ROWS = 256  # rows of each weight in the CPU arms' bounded sample
+REF_DIR = ROOT / "oracle" / "_ref"
+
+
+def _config(args, world: int) -> dict:
+    """The workload description both arms print (identical by construction)."""
+    return {
+        "workload": "llama3-8b linears qkv/o/gate_up/down x tokens {1,8,16,32,64,128}",
+        "tokens": list(args.tokens),
+        "split_k": "persistent stream-K schedule, K ranges summed in-kernel (FP32)",
+        "l2": "no flush: every call reads its own weight copy, ~1.9 GB packed per step "
+              "(inputs larger than the 126 MB L2); calls run back to back between one "
+              "pair of events per step",
+        "parallelism": f"tp{world}" if world > 1 else "single",
+    }
+
+
+def _reference_bridge(name: str):
+    """The reference's own bridge library from oracle/_ref (built from its
+    sources by oracle/Makefile), bound with this package's ABI-2 signature
+    table, or None when it was not built."""
+    import ctypes
+
+    path = REF_DIR / name
+    if not path.is_file():
+        return None
+    from zipserv_asplos26_b200 import runtime
+
+    lib = ctypes.CDLL(str(path))
+    for sym in runtime._SIGNATURES:
+        if hasattr(lib, sym):
+            runtime._bind(lib, sym)
+    return lib if lib.zipserv_abi_version() == 2 else None
 
 
 def _peaks() -> dict:
@@ -262,6 +303,8 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         per_call_pass(zip_call, per_call)
         per_call_pass(dense_call, dense_per_call)
     barrier()
+    ref_gpu, ref_gpu_note = (_reference_gpu_per_call(calls, stream, dev, settle)
+                             if world == 1 else ({}, "single-GPU runs only"))
 
     # End to end through the public API: H2D of activations, GEMM, D2H of
     # outputs, every step. The step's input copies run on one side stream and
@@ -346,15 +389,23 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     value = step_bytes * steps / (zip_total * 1e-3) / 1e9
     peaks = _peaks()
     per_shape = []
+    ours_sum = ref_sum = 0.0
     for c in calls:
         lay, n = c["lay"], c["n"]
         key = (lay["name"], n)
         us = statistics.median(per_call[key]) * 1e3
         dus = statistics.median(dense_per_call[key]) * 1e3
-        per_shape.append({"layer": lay["name"], "m": lay["m"], "k": lay["k"], "n": n,
-                          "zipgemm_us": round(us, 2), "cublas_bf16_us": round(dus, 2),
-                          "gbs": round(call_bytes(c) / (us * 1e-6) / 1e9, 1),
-                          "speedup_vs_cublas": round(dus / us, 3)})
+        row = {"layer": lay["name"], "m": lay["m"], "k": lay["k"], "n": n,
+               "zipgemm_us": round(us, 2), "cublas_bf16_us": round(dus, 2),
+               "gbs": round(call_bytes(c) / (us * 1e-6) / 1e9, 1),
+               "speedup_vs_cublas": round(dus / us, 3)}
+        if key in ref_gpu:
+            rus, rsplit = ref_gpu[key]
+            row.update({"reference_gpu_us": round(rus, 2), "reference_split_k": rsplit,
+                        "speedup_vs_reference_gpu": round(rus / us, 3)})
+            ours_sum += us
+            ref_sum += rus
+        per_shape.append(row)
     traffic = _traffic_record()
     launches = len(calls) * steps
     avg_launch_bytes = step_bytes / len(calls)
@@ -371,16 +422,8 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {
-            "workload": "llama3-8b linears qkv/o/gate_up/down x tokens {1,8,16,32,64,128}",
-            "tokens": list(args.tokens),
-            "split_k": "persistent stream-K schedule, K ranges summed in-kernel (FP32)",
-            "l2": "no flush: every call reads its own weight copy, ~1.9 GB packed per step "
-                  "(inputs larger than the 126 MB L2); calls run back to back between one "
-                  "pair of events per step",
-            "parallelism": f"tp{world}" if world > 1 else "single",
-            "bytes_per_step": int(step_bytes),
-        },
+        "config": _config(args, world),
+        "bytes_per_step": int(step_bytes),
         "roofline": {
             "bound": "hbm",
             "achieved": round(value, 1),
@@ -397,6 +440,13 @@ def run_ours(args, world: int, rank: int) -> dict | None:
             "ms_per_step": round(dense_total / steps, 4),
             "zipgemm_speedup": round(dense_total / zip_total, 3),
         },
+        "reference_gpu": ({
+            "what": "the reference's fused kernel (csrc/L_Kernel.cuh via its CUDA bridge, "
+                    "recompiled for sm_100a) on the same packed weights, best split_k per call",
+            "sum_of_calls_us": round(ref_sum, 1),
+            "zipgemm_sum_of_calls_us": round(ours_sum, 1),
+            "zipgemm_speedup": round(ref_sum / ours_sum, 3),
+        } if ref_gpu else {"unavailable": ref_gpu_note}),
         "e2e": {
             "value": round(step_bytes * steps / (e2e_total * 1e-3) / 1e9, 1),
             "unit": "GB/s",
@@ -444,58 +494,154 @@ def _traffic_record() -> dict:
                     f"{rec.get('launch', 'one launch')}; scaled to the average launch"}
 
 
-def _cpu_case(name: str, n: int, threads: int):
-    """Decode one Llama-3-8B linear on the host and multiply it with n tokens."""
+def _reference_gpu_per_call(calls, stream, dev, settle) -> tuple[dict, str]:
+    """Per-call device time of the reference's own fused kernel on the same
+    packed weights: {(layer, n): (best us, its split_k)}. Every split_k in
+    {1, 2, 4, 8} that divides K/64 is timed in passes over all calls back to
+    back (each call reading its own weight copy, as in the other per-call
+    passes); the reference's outputs are checked against ours."""
+    import torch
+
+    from zipserv_asplos26_b200 import runtime
+
+    lib = _reference_bridge("libzipserv_ref_cuda.so")
+    if lib is None or not hasattr(lib, "zipserv_mm"):
+        return {}, "the reference CUDA bridge is not built (make -C oracle ref-cuda)"
+    ws = torch.empty(max(8 * c["n"] * c["lay"]["m"] for c in calls), dtype=torch.bfloat16,
+                     device=dev)
+    outs = [torch.empty_like(c["out"]) for c in calls]
+    handle = stream.cuda_stream
+
+    def launch(i, c, split):
+        pk = c["packed"]
+        status = lib.zipserv_mm(handle, *(b.data_ptr() for b in pk.buffers), pk.max_common,
+                                pk.max_rare, pk.start_exp, c["x"].data_ptr(), outs[i].data_ptr(),
+                                c["lay"]["m"], c["n"], c["lay"]["k"],
+                                ws.data_ptr() if split > 1 else None, split)
+        if status:
+            raise SystemExit(f"reference zipserv_mm failed ({status}) on {c['lay']['name']}")
+
+    times: dict = {}
+    for split in (1, 2, 4, 8):
+        todo = [(i, c) for i, c in enumerate(calls) if (c["lay"]["k"] // 64) % split == 0]
+        for i, c in todo:  # warm-up
+            launch(i, c, split)
+        for _ in range(3):
+            events = []
+            settle()
+            for i, c in todo:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(stream)
+                launch(i, c, split)
+                e.record(stream)
+                events.append((c, s, e))
+            torch.cuda.synchronize(dev)
+            for c, s, e in events:
+                times.setdefault((c["lay"]["name"], c["n"], split), []).append(s.elapsed_time(e))
+        # The reference's result must agree with ours (FP32 sums, BF16 output).
+        for i, c in todo:
+            ours = runtime.linear_kparts(c["x"], c["packed"], 0).float()
+            err = (outs[i].float() - ours).abs().max().item() / max(ours.abs().max().item(), 1e-30)
+            if err > 2e-2:
+                raise SystemExit(f"reference kernel disagrees on {c['lay']['name']} n={c['n']}")
+    best = {}
+    for (name, n, split), ts in times.items():
+        us = statistics.median(ts) * 1e3
+        if (name, n) not in best or us < best[(name, n)][0]:
+            best[(name, n)] = (us, split)
+    return best, ""
+
+
+def _cpu_sweep(args, threads: int):
+    """The sweep's bounded CPU sample: for every layer the first
+    CPU_SAMPLE_ROWS rows of its weight, packed by the reference's own encoder
+    (oracle/_ref; the oracle restatement when it was not built here), and for
+    every token count one decode + FP32 GEMM of that sample (oracle/, the
+    restated reference CPU decoder and GEMM loop). Returns (run_step,
+    bytes_per_step, pack_seconds, pack_kind)."""
+    import ctypes
+
     import numpy as np
     import torch
 
     from oracle import oracle
+    from zipserv_asplos26_b200 import runtime
 
-    spec = {lay[0]: lay for lay in LAYERS}[name]
-    _, m, k, _ = spec
-    g = torch.Generator().manual_seed(1000 + [lay[0] for lay in LAYERS].index(name))
-    w = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
-    packed = oracle.pack(w)
-    x = torch.randn(n, k, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
-    xw = x.view(torch.int16).numpy().view(np.uint16)
-    storage = sum(b.nbytes for b in packed.abi_buffers())
+    ref = _reference_bridge("libzipserv_ref_cpu.so")
+    samples, pack_s = [], 0.0
+    for li, (name, m, k, _split) in enumerate(LAYERS):
+        g = torch.Generator().manual_seed(1000 + li)
+        full = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16)
+        w = full[:CPU_SAMPLE_ROWS].contiguous().view(torch.int16).numpy().view(np.uint16)
+        del full
+        t0 = time.perf_counter()
+        if ref is not None:
+            desc = runtime._Descriptor()
+            runtime._check(0 if ref.zipserv_compress(w.ctypes.data, w.shape[0], k,
+                                                     ctypes.byref(desc)) == 0 else -1)
+            bufs = [np.ctypeslib.as_array(ctypes.cast(desc.buffers[i], ctypes.POINTER(
+                ctypes.c_uint8)), shape=(int(desc.lengths[i]),)).copy() if desc.lengths[i]
+                else np.zeros(0, np.uint8) for i in range(7)]
+            start_exp = desc.start_exp
+            ref.zipserv_free(ctypes.byref(desc))
+        else:
+            packed = oracle.pack(w)
+            bufs, start_exp = packed.abi_buffers(), packed.start_exp
+        pack_s += time.perf_counter() - t0
+        for n in args.tokens:
+            x = torch.randn(n, k, generator=torch.Generator().manual_seed(7 + n)).to(
+                torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+            nbytes = sum(b.nbytes for b in bufs) + 2 * n * k + 2 * n * w.shape[0]
+            samples.append((bufs, w.shape[0], k, start_exp, x, nbytes))
 
-    def run():
-        dec = oracle.decode(packed.abi_buffers(), m, k, packed.start_exp, threads=threads)
-        oracle.gemm(dec, xw, threads=threads)
+    def run_step():
+        for bufs, m, k, start_exp, x, _ in samples:
+            dec = oracle.decode(bufs, m, k, start_exp, threads=threads)
+            oracle.gemm(dec, x, threads=threads)
 
-    return run, storage + 2 * n * k + 2 * n * m
+    kind = "reference" if ref is not None else "port"
+    return run_step, sum(s[-1] for s in samples), pack_s, kind
+
+
+def _sample_text(pack_kind: str) -> str:
+    packer = ("the reference's own encoder built from its sources (oracle/_ref)"
+              if pack_kind == "reference" else "the oracle restatement of the encoder")
+    return (f"per step all 24 calls of the sweep, each on the first {CPU_SAMPLE_ROWS} rows of "
+            f"its weight: packed once by {packer}, then decoded and multiplied in FP32 by "
+            f"oracle/'s restatement of the reference CPU decoder and GEMM loop")
 
 
 def cpu_baseline(args) -> dict:
     threads = os.cpu_count() or 1
-    run, nbytes = _cpu_case("o", 8, threads)
-    run()
+    run_step, nbytes, pack_s, pack_kind = _cpu_sweep(args, threads)
+    run_step()
     t0 = time.perf_counter()
     reps = 0
-    while reps < 3 or time.perf_counter() - t0 < 10.0:
-        run()
+    while reps < 2 or time.perf_counter() - t0 < 10.0:
+        run_step()
         reps += 1
         if time.perf_counter() - t0 > 30.0:
             break
     dt = time.perf_counter() - t0
+    sample_weights = CPU_SAMPLE_ROWS * sum(lay[2] for lay in LAYERS)
     return {"value": round(nbytes * reps / dt / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port",
-            "sample": f"o-proj 4096x4096 decode + FP32 GEMM with 8 tokens, {reps} repetitions "
-                      f"({dt:.1f} s), oracle/ restatement of the reference CPU decoder and GEMM"}
+            "pack": {"kind": pack_kind, "seconds_for_4_samples": round(pack_s, 4),
+                     "weights_per_s": round(sample_weights / pack_s, 1)},
+            "sample": _sample_text(pack_kind) + f"; {reps} steps in {dt:.1f} s"}
 
 
 def run_reference(args, world: int, rank: int) -> dict | None:
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
-    run, nbytes = _cpu_case("o", 8, threads)
+    run_step, nbytes, pack_s, pack_kind = _cpu_sweep(args, threads)
     for _ in range(args.warmup):
-        run()
+        run_step()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        run()
+        run_step()
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = nbytes * len(times) / total / 1e9
@@ -503,14 +649,15 @@ def run_reference(args, world: int, rank: int) -> dict | None:
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
         "impl": "reference",
-        "config": {"workload": "llama3-8b o-proj 4096x4096, 8 tokens (bounded CPU sample of the "
-                               "decode sweep)", "parallelism": "host cores"},
+        "config": _config(args, world),
+        "bytes_per_step": nbytes,
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port",
-                         "sample": "per step: decode the packed o-proj weight and an FP32 GEMM "
-                                   "with 8 tokens (oracle/ restatement of the reference CPU path)"},
+                         "pack": {"kind": pack_kind, "seconds_for_4_samples": round(pack_s, 4)},
+                         "sample": _sample_text(pack_kind)},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -12,9 +12,11 @@
 // Weight reconstruction is bit-exact; GEMM sums are FP32 and may round
 // differently from another backend.
 //
-// Difference from the reference, by design: Split-K partial sums are reduced
-// inside the kernel in FP32 over distributed shared memory. The workspace
-// argument is still validated (required when Split_K > 1) but never written.
+// Difference from the reference, by design: the K reduction runs inside the
+// fused kernel in FP32 (partial pieces exchanged between CTAs through L2 and
+// added in a fixed order), not in a second kernel over a Split_K workspace.
+// The workspace argument is still validated (required when Split_K > 1) but
+// never written.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

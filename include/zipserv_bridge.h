@@ -16,9 +16,9 @@
  *     can be captured in CUDA graphs. The only device allocation is the
  *     GEMM's K-range scratch: zipserv_mm, zipserv_mm_fp32 and
  *     zipserv_mm_kparts keep one library-owned buffer per (device, stream),
- *     allocated on the first launch that needs it and grown on demand, never
- *     while the stream is being captured (run a shape once before capturing
- *     it); zipserv_mm_ws takes the scratch from the caller instead.
+ *     allocated on the first launch that needs it (sized for every shape of the
+ *     default schedule, also under stream capture) and never freed; zipserv_mm_ws
+ *     takes the scratch from the caller instead.
  *   - Return 0 (cudaSuccess) or a cudaError_t value; on failure
  *     zipserv_error() describes it. Contract violations, including null
  *     pointers and device buffers not aligned to 16 bytes, return
@@ -112,7 +112,8 @@ int zipserv_mm_workspace_size(int m, int n, int k, int k_parts, uint64_t* partia
  * before its first use; every launch returns the counters it used to zero,
  * so one pair of buffers (sized for the largest shape) serves any sequence
  * of launches, as long as no two of them run at the same time. Both may be
- * null when the sizes are 0. */
+ * null when the sizes are 0. After zipserv_device_flags reports bit 0 (a
+ * launch gave up on a wait), zero the counters again before the next call. */
 int zipserv_mm_ws(void* stream, const void* sm, const void* rare, const void* b1,
                   const void* b2, const void* b3, const void* medium, const void* global,
                   int max_common, int max_rare, int start_exp, const void* x, void* y, int m,
@@ -138,6 +139,16 @@ int zipserv_mm_noalloc(void* stream, const void* sm, const void* rare, const voi
 /* The K partition zipserv_mm picks for this shape on the current device, or
  * a negative value if the shape is invalid. */
 int zipserv_mm_plan(int m, int n, int k);
+
+/* No counterpart in the reference. Sets how long (nanoseconds) the CTA that
+ * holds the first K part of a split row block waits for the other parts'
+ * FP32 pieces before it publishes its own part instead and leaves the sum to
+ * the last part to arrive (default 50000; that happens when the other CTAs
+ * could not start, e.g. other work holds SMs). Both ways sum in the same K
+ * order, so outputs are identical; 0 makes every split row block take the
+ * last-arrival route (tests use it). Applies to later launches; returns the
+ * previous value. */
+uint64_t zipserv_mm_reducer_wait(uint64_t ns);
 
 /* Device-side failure flags of the current device (bit 0: a pipeline wait
  * in a kernel gave up after its iteration limit; results of that launch are

@@ -193,6 +193,8 @@ extern "C" int zipserv_mm_plan(int m, int n, int k) {
     return zs::plan_kparts(m, n, k, device);
 }
 
+extern "C" uint64_t zipserv_mm_reducer_wait(uint64_t ns) { return zs::set_reducer_wait_ns(ns); }
+
 extern "C" int zipserv_device_flags(unsigned* flags, int clear) {
     if (!flags) return int(cudaErrorInvalidValue);
     cudaError_t e = cudaMemcpyFromSymbol(flags, zs::g_device_flags, sizeof(unsigned));

@@ -114,9 +114,13 @@ __device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
 }
 
 // Bounded wait until the global word at `p` (written by other CTAs with
-// release semantics) reaches `value`: acquire loads, two-second limit, then
-// sets g_device_flags bit 0 and returns false.
-__device__ __forceinline__ bool wait_global_geq(const uint32_t* p, uint32_t value) {
+// release semantics) reaches `value`: acquire loads, gives up after
+// `limit_ns` and returns false. With `flag` set, giving up also raises
+// g_device_flags bit 0 (a wait that must not expire); without it the caller
+// has a fallback for the case.
+__device__ __forceinline__ bool wait_global_geq(const uint32_t* p, uint32_t value,
+                                                uint64_t limit_ns = 2000000000ull,
+                                                bool flag = true) {
     uint64_t start = 0;
     for (uint32_t i = 0; i < (1u << 30); ++i) {
         uint32_t v;
@@ -125,12 +129,21 @@ __device__ __forceinline__ bool wait_global_geq(const uint32_t* p, uint32_t valu
         if ((i & 15) == 15) {
             const uint64_t now = global_timer_ns();
             if (!start) start = now;
-            else if (now - start > 2000000000ull) break;
+            else if (now - start > limit_ns) break;
             __nanosleep(64);
         }
     }
-    atomicOr(&g_device_flags, 1u);
+    if (flag) atomicOr(&g_device_flags, 1u);
     return false;
+}
+// Acquire-release increment of a global counter; returns the prior value.
+__device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t* p, uint32_t v) {
+    uint32_t prior;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                 : "=r"(prior)
+                 : "l"(p), "r"(v)
+                 : "memory");
+    return prior;
 }
 // Release increment of a global counter (orders this thread's earlier writes
 // before the increment for any CTA that acquires the counter).

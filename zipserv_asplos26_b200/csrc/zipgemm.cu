@@ -27,10 +27,12 @@
 // Split-K: the grid is persistent (one CTA per SM) and every CTA takes an
 // equal contiguous range of the (row block, K slice) work items, so each
 // gets the same amount of decoding whatever the shape. A row block whose K
-// range is split over several CTAs is summed through an FP32 workspace by
-// the last CTA to finish a piece of it, in K order (deterministic). No CTA
-// waits for another and no second kernel runs (replaces
-// csrc/Reduction_Kernel.cuh:16-41).
+// range is split over several CTAs is summed in FP32, in K order
+// (deterministic), inside this kernel: the CTA holding its first K part
+// waits a bounded time for the other parts' pieces (published through L2)
+// and adds them to its TMEM accumulator; if they are late, it publishes its
+// own part instead and the last part to arrive reduces. No second kernel
+// runs (replaces csrc/Reduction_Kernel.cuh:16-41).
 //
 // Reference kernel this replaces: csrc/L_Kernel.cuh:310-915 (mma.sync,
 // cp.async double buffering, per-column-warp redundant decode).
@@ -58,6 +60,13 @@ namespace zs {
 // groups; NDG + 1 = epilogue.
 constexpr int gemm_threads(int ndg) { return 256 + 128 * ndg; }
 
+// Default of how long a reducing CTA waits for the other K parts of its row
+// block before it falls back to publishing its own part (the last arrival
+// then reduces). On a resident grid the other parts are their CTAs' first
+// segments and arrive long before; the limit only matters when those CTAs
+// could not start (other work holding SMs).
+constexpr uint64_t kReducerWaitNs = 50000;
+
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
 __host__ __device__ __forceinline__ int lane_row(int slot) {
@@ -75,11 +84,15 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
 // [start(c), start(c+1)), start(c) = c * steps / grid: every CTA gets the
 // same number of K slices (+-1) whatever the shape. The run of a CTA's items
 // inside one unit is a segment. A segment that covers its whole unit stores
-// BF16 output directly; a partial segment writes its FP32 partial tile to the
-// workspace, and the CTA that delivers a piece's last partial (an arrival
-// counter per unit piece) sums that piece's partials in K order - a fixed
-// order, so results do not depend on timing - converts and stores it, and
-// resets the counter. No CTA ever waits for another.
+// BF16 output directly. For a unit split over CTAs c0 .. c0 + parts - 1,
+// parts 1 .. are their CTAs' first segments and write FP32 partial pieces to
+// the workspace, then count their arrival (one counter per (c0, TMEM lane
+// quarter)); part 0 is c0's last segment. On a resident grid c0 waits,
+// bounded, for the other arrivals and sums its TMEM accumulator with their
+// pieces; if it gives up (or the grid is larger than the GPU) it publishes
+// too and whichever part arrives last sums all pieces. Either way the sum
+// runs in K order - a fixed order, so results do not depend on timing - and
+// the reducer returns the counter to zero.
 __device__ __forceinline__ int step_start(int c, const GemmParams& p) {
     return int(int64_t(c) * p.steps / p.grid);
 }
@@ -148,27 +161,23 @@ struct ChunkReduce {
 };
 
 // A decoder warp's share of its CTA's last-segment reduction (kept out of
-// line so the decoder loop's register allocation is not affected).
-__device__ __noinline__ void help_reduce(float* ws_partials, uint16_t* y, uint32_t* ws_counters,
-                                         int m, int n, int bn, int pieces, uint32_t tmem_cols,
-                                         int grid, int steps, uint32_t tmem, uint32_t bar_d,
-                                         int unit, int s, int rbs, int kt, int cta, int g, int q,
-                                         int lane, int stride) {
+// line so the decoder loop's register allocation is not affected). Runs
+// only when the quarter's epilogue warp saw every other part arrive in time.
+__device__ __noinline__ void help_reduce(float* ws_partials, uint16_t* y, int m, int n, int bn,
+                                         int pieces, uint32_t tmem_cols, int grid, int steps,
+                                         uint32_t tmem, uint32_t bar_d, int unit, int s, int rbs,
+                                         int kt, int cta, int g, int q, int lane, int stride) {
     const int b = s & 1, chunks = bn / 16, ubeg = unit * kt;
     const bool dok = ptx::mbar_wait(bar_d + 8u * uint32_t(b), uint32_t(s >> 1) & 1u);
     ptx::tc_fence_after();
     ptx::wait_prerequisites();  // output writes, as in the epilogue
     const int last_owner = int((int64_t(ubeg + kt - 1 + 1) * grid - 1) / steps);
     const int parts = last_owner - cta + 1;
-    uint32_t* quarter = ws_counters + size_t(unit) * 4u + size_t(q);
-    bool wok = true;
-    if (lane == 0) wok = ptx::wait_global_geq(quarter, uint32_t(parts - 1));
-    wok = __shfl_sync(kFullMask, wok, 0);
     const int mrow = (unit % rbs) * 128 + lane_row(32 * q + lane);
     const ChunkReduce cr{ws_partials, y, m, n, bn, pieces,
                          tmem + (uint32_t(32 * q) << 16) + uint32_t(b) * tmem_cols,
                          cta, parts, unit / rbs, mrow, lane, size_t(q) * size_t(chunks),
-                         mrow < m, dok, wok};
+                         mrow < m, dok, true};
     for (int c = g + 1; c < chunks; c += stride) cr.run(c);
     ptx::tc_fence_before();
 }
@@ -196,6 +205,9 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     const uint32_t bar_tempty = bar_d + 16;                    // [2] accumulator drained
     const uint32_t bar_tab = bar_tempty + 16;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + (bar_tab - sbase) + 8);
+    // Per TMEM lane quarter: 1 when a reducing CTA's other K parts arrived in
+    // time (written by the quarter's epilogue warp, read by its decoder warps).
+    const uint32_t verdict = sbase + 512;
     const uint32_t tables = sbase + kBarrierBytes;
     constexpr int kEpiWarp = 4 + 4 * NDG;
 
@@ -502,16 +514,19 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         // If the CTA's last segment is a row block it reduces (resident
         // grids), help the epilogue warp of lane quarter q with it: group g
         // takes chunks g + 1, g + 2 + NDG, ... . Every warp of the quarter
-        // meets at the quarter's named barrier, chunks or not.
+        // meets twice at the quarter's named barrier: once for the epilogue
+        // warp's verdict on the other parts (all arrived in time, or the
+        // reduction falls back to the last arrival), once when done.
         if (p.resident && nseg > 0 && p.bn > 16) {
             const int s = nseg - 1, unit = unit0 + s, ubeg = unit * kt;
             const bool whole = t_begin <= ubeg && ubeg + kt <= t_end;
             if (!whole && cta == step_owner(ubeg, p)) {
                 const int chunks = p.bn / 16;
-                if (g + 1 < chunks)
-                    help_reduce(p.ws_partials, p.y, p.ws_counters, p.m, p.n, p.bn, p.pieces,
-                                p.tmem_cols, p.grid, p.steps, tmem, bar_d, unit, s, rbs, kt, cta,
-                                g, q, lane, 1 + NDG);
+                ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
+                const bool fast = ptx::lds_s32(verdict + 4u * uint32_t(q)) != 0;
+                if (fast && g + 1 < chunks)
+                    help_reduce(p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, p.tmem_cols, p.grid,
+                                p.steps, tmem, bar_d, unit, s, rbs, kt, cta, g, q, lane, 1 + NDG);
                 ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
             }
         }
@@ -565,69 +580,47 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             const size_t piece0 = size_t(q) * size_t(chunks);  // this quarter's pieces
             const int c0 = step_owner(ubeg, p);
             const int parts = step_owner(ubeg + kt - 1, p) - c0 + 1;
-            // Partial pp of a piece: CTA c0 + pp, slot 1 only when the unit
-            // starts inside that CTA's range after its first segment.
-            auto partial = [&](int pp, int c) {
-                const int cp = c0 + pp;
-                const int wh = (pp == 0 && step_start(cp, p) < ubeg) ? 1 : 0;
-                return p.ws_partials +
-                       ((size_t(cp) * 2 + size_t(wh)) * size_t(p.pieces) + piece0 + size_t(c)) *
-                           512u +
-                       size_t(lane) * 16u;
-            };
-            // acc += partials first .. parts - 1 of piece c, summed in K
-            // order. Two partials (all 16 values of each) are loaded per
-            // round trip to L2.
-            auto add_partials = [&](int c, int first, float (&acc)[16]) {
-                for (int pp = first; pp < parts; pp += 2) {
-                    const bool two = pp + 1 < parts;
-                    const float* s0 = partial(pp, c);
-                    const float* s1 = two ? partial(pp + 1, c) : s0;
-                    float4 x[4], y[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) x[i] = ptx::ldg_cg_f4(s0 + 4 * i);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) y[i] = ptx::ldg_cg_f4(s1 + 4 * i);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        acc[4 * i] += x[i].x, acc[4 * i + 1] += x[i].y;
-                        acc[4 * i + 2] += x[i].z, acc[4 * i + 3] += x[i].w;
-                    }
-                    if (two) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            acc[4 * i] += y[i].x, acc[4 * i + 1] += y[i].y;
-                            acc[4 * i + 2] += y[i].z, acc[4 * i + 3] += y[i].w;
-                        }
-                    }
-                }
-            };
+            // One arrival counter per (first CTA of the unit, lane quarter):
+            // a CTA is the first part of at most one split unit (its last
+            // segment), so grid x 4 counters serve any shape.
+            uint32_t* ctr = p.ws_counters + size_t(c0) * 4u + size_t(q);
             if (p.resident && cta == c0) {
                 // This CTA holds the unit's first K part, the last one it
-                // computes: it reduces the unit once the other parts (each
-                // their CTA's first segment, so never waiting on this one)
-                // have published their quarter-q pieces.
-                uint32_t* quarter = p.ws_counters + size_t(unit) * 4u + size_t(q);
-                bool wok = true;
-                if (lane == 0) wok = ptx::wait_global_geq(quarter, uint32_t(parts - 1));
-                wok = __shfl_sync(kFullMask, wok, 0);
-                // Chunks 0, 1 + NDG, ...; the quarter's decoder warps take the
-                // others (this is the CTA's last segment, so they are idle).
-                const ChunkReduce cr{p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, tbase, c0, parts,
-                                     nb, mrow, lane, piece0, row_ok, dok, wok};
-                // With one chunk (N tile 16) the epilogue warp works alone.
-                const int stride = chunks > 1 ? 1 + NDG : 1;
-                for (int c = 0; c < chunks; c += stride) cr.run(c);
-                ptx::tc_fence_before();
-                // Every warp of the quarter has read the counter before it is reset.
-                if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
-                else __syncwarp();
-                if (lane == 0) {
-                    ptx::mbar_arrive(bar_addr(bar_tempty, b));
-                    *reinterpret_cast<volatile uint32_t*>(quarter) = 0u;  // ready for reuse
+                // computes. The other parts are their CTAs' first segments,
+                // so on a resident grid they publish early: wait (briefly)
+                // for them and reduce with this part straight from TMEM. If
+                // they are late (their CTAs could not start because other
+                // work holds SMs), publish this part like the others instead:
+                // the last arrival reduces, so no CTA depends on another one
+                // being resident.
+                bool fast = true;
+                if (lane == 0)
+                    fast = ptx::wait_global_geq(ctr, uint32_t(parts - 1), p.reducer_wait_ns, false);
+                fast = __shfl_sync(kFullMask, fast, 0);
+                if (chunks > 1) {  // tell the quarter's decoder warps
+                    if (lane == 0) ptx::sts32(verdict + 4u * uint32_t(q), fast ? 1u : 0u);
+                    ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
                 }
-                continue;
+                if (fast) {
+                    // Chunks 0, 1 + NDG, ...; the quarter's decoder warps take
+                    // the others (this is the CTA's last segment, they are idle).
+                    const ChunkReduce cr{p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, tbase, c0,
+                                         parts, nb, mrow, lane, piece0, row_ok, dok, true};
+                    // With one chunk (N tile 16) the epilogue warp works alone.
+                    const int stride = chunks > 1 ? 1 + NDG : 1;
+                    for (int c = 0; c < chunks; c += stride) cr.run(c);
+                    ptx::tc_fence_before();
+                    if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
+                    else __syncwarp();
+                    if (lane == 0) {
+                        ptx::mbar_arrive(bar_addr(bar_tempty, b));
+                        *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
+                    }
+                    continue;
+                }
+                if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
             }
+            // Publish this part's FP32 pieces of the quarter.
             float* mine = p.ws_partials +
                           ((size_t(cta) * 2 + size_t(which)) * size_t(p.pieces) + piece0) * 512u +
                           size_t(lane) * 16u;
@@ -648,32 +641,38 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             // lane 0's release below, which publishes them GPU-wide.
             __syncwarp();
             if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));  // TMEM read
-            if (p.resident) {
-                if (lane == 0)
-                    ptx::red_release_add(p.ws_counters + size_t(unit) * 4u + size_t(q), 1u);
-                continue;
-            }
-            __threadfence();  // each lane's partials visible before its arrival counts
-            __syncwarp();
-            // Not every CTA resident: whoever delivers a piece's last partial
-            // reduces it.
-            uint32_t* counters = p.ws_counters + size_t(unit) * size_t(p.pieces) + piece0;
-            // Lane c counts this CTA's arrival at piece c.
-            const uint32_t prior = lane < chunks ? atomicAdd(counters + lane, 1u) : 0u;
-            const uint32_t last = __ballot_sync(kFullMask, lane < chunks && prior == uint32_t(parts - 1));
-            if (!last) continue;
-            __threadfence();  // every partial of those pieces is visible now
-            for (uint32_t todo = last; todo; todo &= todo - 1) {
-                const int c = __ffs(todo) - 1;
+            // Count this arrival. On a resident grid the first part's CTA is
+            // normally waiting (it never adds), so no writer is last; when it
+            // gave up waiting, or the grid is not resident, the last arrival
+            // sums every part in K order, stores, and resets the counter.
+            uint32_t prior = 0;
+            if (lane == 0) prior = ptx::atom_acq_rel_add(ctr, 1u);
+            if (__shfl_sync(kFullMask, prior, 0) != uint32_t(parts - 1)) continue;
+            __threadfence();  // every lane sees every part's pieces
+            for (int c = 0; c < chunks; ++c) {
                 float acc[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-                add_partials(c, 0, acc);
+                for (int pp = 0; pp < parts; ++pp) {
+                    const int cp = c0 + pp;
+                    // Part pp is CTA c0 + pp's first segment (slot 0), except
+                    // the first part when the unit starts after that CTA's
+                    // first segment (slot 1).
+                    const int wh = (pp == 0 && step_start(cp, p) < ubeg) ? 1 : 0;
+                    const float* src = p.ws_partials +
+                                       ((size_t(cp) * 2 + size_t(wh)) * size_t(p.pieces) +
+                                        piece0 + size_t(c)) * 512u + size_t(lane) * 16u;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 v = ptx::ldg_cg_f4(src + 4 * i);
+                        acc[4 * i] += v.x, acc[4 * i + 1] += v.y;
+                        acc[4 * i + 2] += v.z, acc[4 * i + 3] += v.w;
+                    }
+                }
                 if (row_ok) store_row(nb, c, mrow, acc);
             }
             __syncwarp();
-            if ((last >> lane) & 1u)
-                *reinterpret_cast<volatile uint32_t*>(counters + lane) = 0u;  // ready for reuse
+            if (lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
         }
     }
 
@@ -889,20 +888,33 @@ static Schedule make_schedule(int m, int n, int k, int kparts, int sms) {
     return s;
 }
 
-// Fixup scratch of a schedule: FP32 partial tiles (any contents) and one
-// arrival counter per unit piece. Counters live in their own buffer, which
-// holds zeros between launches (a launch returns every counter it used to
-// zero), so launches of different shapes can share both buffers.
+// Fixup scratch of a schedule: FP32 partial tiles (any contents; at most two
+// partial segments per CTA, its first and last) and one arrival counter per
+// (CTA, TMEM lane quarter). Counters live in their own buffer, which holds
+// zeros between launches (the launch that completes a unit returns its
+// counter to zero), so launches of different shapes can share both buffers.
 static size_t schedule_partial_bytes(const Schedule& s) {
     return s.partial ? size_t(s.grid) * 2u * size_t(s.pieces) * 512u * sizeof(float) : 0;
 }
 static size_t schedule_counter_bytes(const Schedule& s) {
-    return s.partial ? (size_t(s.units) * size_t(s.pieces) * 4u + 15u) / 16u * 16u : 0;
+    return s.partial ? (size_t(s.grid) * 4u * 4u + 15u) / 16u * 16u : 0;
 }
 
 // Library-owned fixup scratch, one pair of buffers per (device, stream):
-// launches on one stream are ordered, so they can share it. Grown (never
-// shrunk) on demand; growth is refused while the stream is being captured.
+// launches on one stream are ordered, so they can share it. The first launch
+// that needs scratch on a stream allocates enough for every shape of the
+// default schedule (one CTA per SM, N tile 256: 2 x 64 pieces of 2 KB per
+// CTA, 38.8 MB on a 148-SM GPU), so later shapes never allocate. Only an
+// explicit K partition with more CTAs than SMs can need more; buffers that
+// are outgrown are kept (never freed: launches already queued or captured
+// in a graph may still use them), so no launch ever waits for the stream.
+// An allocation while the stream is being captured switches this thread to
+// relaxed capture mode for the cudaMalloc (it enqueues nothing); the
+// counters' zero-fill is then captured with the launch, so the first launch
+// on the stream outside capture enqueues it once more. A graph keeps using
+// the scratch of the stream it was captured on: replaying it while other
+// work uses that stream's scratch (on any stream) races, as with any
+// library workspace captured in a graph.
 struct WorkspaceEntry {
     int device;
     cudaStream_t stream;
@@ -910,56 +922,75 @@ struct WorkspaceEntry {
     size_t partial_bytes;
     void* counters;
     size_t counter_bytes;
+    bool zero_pending;  // counters zero-filled only inside a captured graph so far
 };
 std::vector<WorkspaceEntry> g_workspaces;
+std::vector<void*> g_retired_workspaces;
 std::mutex g_workspace_mutex;
 
-static cudaError_t library_workspace(int device, cudaStream_t stream, size_t partial_bytes,
-                                     size_t counter_bytes, void** partials, void** counters) {
+static cudaError_t relaxed_malloc(void** ptr, size_t bytes) {
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaError_t e = cudaThreadExchangeStreamCaptureMode(&mode);
+    if (e != cudaSuccess) return e;
+    const cudaError_t a = cudaMalloc(ptr, bytes);
+    e = cudaThreadExchangeStreamCaptureMode(&mode);  // restores the caller's mode
+    return a != cudaSuccess ? a : e;
+}
+
+static cudaError_t library_workspace(int device, int sms, cudaStream_t stream,
+                                     size_t partial_bytes, size_t counter_bytes,
+                                     void** partials, void** counters) {
     std::lock_guard<std::mutex> lock(g_workspace_mutex);
     WorkspaceEntry* entry = nullptr;
     for (WorkspaceEntry& e : g_workspaces)
         if (e.device == device && e.stream == stream) entry = &e;
     if (!entry) {
-        g_workspaces.push_back({device, stream, nullptr, 0, nullptr, 0});
+        g_workspaces.push_back({device, stream, nullptr, 0, nullptr, 0, false});
         entry = &g_workspaces.back();
     }
-    if (entry->partial_bytes < partial_bytes || entry->counter_bytes < counter_bytes) {
-        cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &status) != cudaSuccess ||
-            status != cudaStreamCaptureStatusNone) {
-            zs_set_error("zipgemm: K-range scratch must be allocated outside stream capture "
-                         "(run this shape once on the stream before capturing it)");
-            return cudaErrorStreamCaptureUnsupported;
+    const size_t full_p = size_t(sms) * 2u * 64u * 512u * sizeof(float);
+    const size_t full_c = (size_t(sms) * 16u + 15u) / 16u * 16u;
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(stream, &capture);
+    if (e != cudaSuccess) return e;
+    const bool capturing = capture != cudaStreamCaptureStatusNone;
+    if (entry->partial_bytes < partial_bytes) {
+        const size_t bytes = std::max(partial_bytes, full_p);
+        void* fresh = nullptr;
+        if ((e = relaxed_malloc(&fresh, bytes)) != cudaSuccess) {
+            zs_set_error("zipgemm: could not allocate K-range scratch");
+            return e;
         }
-        // Launches already queued may still use the old buffers.
-        cudaError_t e = cudaStreamSynchronize(stream);
-        if (e != cudaSuccess) return e;
-        if (entry->partial_bytes < partial_bytes) {
-            cudaFree(entry->partials);
-            entry->partials = nullptr, entry->partial_bytes = 0;
-            if ((e = cudaMalloc(&entry->partials, partial_bytes)) != cudaSuccess) {
-                zs_set_error("zipgemm: could not allocate K-range scratch");
-                return e;
-            }
-            entry->partial_bytes = partial_bytes;
+        if (entry->partials) g_retired_workspaces.push_back(entry->partials);
+        entry->partials = fresh, entry->partial_bytes = bytes;
+    }
+    if (entry->counter_bytes < counter_bytes) {
+        const size_t bytes = std::max(counter_bytes, full_c);
+        void* fresh = nullptr;
+        if ((e = relaxed_malloc(&fresh, bytes)) != cudaSuccess) {
+            zs_set_error("zipgemm: could not allocate K-range counters");
+            return e;
         }
-        if (entry->counter_bytes < counter_bytes) {
-            cudaFree(entry->counters);
-            entry->counters = nullptr, entry->counter_bytes = 0;
-            if ((e = cudaMalloc(&entry->counters, counter_bytes)) != cudaSuccess) {
-                zs_set_error("zipgemm: could not allocate K-range counters");
-                return e;
-            }
-            if ((e = cudaMemsetAsync(entry->counters, 0, counter_bytes, stream)) != cudaSuccess)
-                return e;
-            entry->counter_bytes = counter_bytes;
+        if ((e = cudaMemsetAsync(fresh, 0, bytes, stream)) != cudaSuccess) {
+            g_retired_workspaces.push_back(fresh);
+            return e;
         }
+        if (entry->counters) g_retired_workspaces.push_back(entry->counters);
+        entry->counters = fresh, entry->counter_bytes = bytes;
+        entry->zero_pending = capturing;
+    } else if (entry->zero_pending && !capturing) {
+        if ((e = cudaMemsetAsync(entry->counters, 0, entry->counter_bytes, stream)) != cudaSuccess)
+            return e;
+        entry->zero_pending = false;
     }
     *partials = entry->partials;
     *counters = entry->counters;
     return cudaSuccess;
 }
+
+std::atomic<uint64_t> g_reducer_wait_ns{kReducerWaitNs};
+
+uint64_t set_reducer_wait_ns(uint64_t ns) { return g_reducer_wait_ns.exchange(ns); }
 
 int plan_kparts(int m, int n, int k, int device) {
     if (!valid_matrix(m, k) || n <= 0) return -1;
@@ -998,8 +1029,12 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.row_blocks = sched.row_blocks, p.units = sched.units, p.steps = sched.steps;
     p.grid = sched.grid, p.pieces = sched.pieces;
     // One CTA per SM (the shared-memory footprint allows no more): with at
-    // most one CTA per SM every CTA of the grid runs at the same time.
+    // most one CTA per SM every CTA of the grid normally runs at the same
+    // time, and a row block's first part may wait (briefly) for the others.
+    // Nothing depends on it: a reducer that waits in vain falls back to the
+    // last-arrival reduction.
     p.resident = sched.grid <= d.sms ? 1 : 0;
+    p.reducer_wait_ns = g_reducer_wait_ns.load(std::memory_order_relaxed);
     p.bn = sched.bn;
     if (sched.partial) {
         const size_t need_p = schedule_partial_bytes(sched), need_c = schedule_counter_bytes(sched);
@@ -1013,7 +1048,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
                 return cudaErrorInvalidValue;
             }
             partials = scratch->partials, counters = scratch->counters;
-        } else if ((e = library_workspace(device, stream, need_p, need_c, &partials,
+        } else if ((e = library_workspace(device, d.sms, stream, need_p, need_c, &partials,
                                           &counters)) != cudaSuccess) {
             return e;
         }

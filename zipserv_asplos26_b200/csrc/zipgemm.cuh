@@ -38,7 +38,7 @@ struct GemmParams {
     const int* global;
     uint16_t* y;           // [n, m] BF16
     float* ws_partials;    // [grid][2][pieces][32 lanes][16] FP32 partial tiles
-    uint32_t* ws_counters;  // [units][pieces] arrivals (zero between launches)
+    uint32_t* ws_counters;  // [grid][4 lane quarters] arrivals (zero between launches)
     int m, n, k;
     int kt;                // k / 64
     int row_tiles;         // m / 64
@@ -60,6 +60,7 @@ struct GemmParams {
     uint32_t x_bytes;      // one x slot: bn tokens x one K slice (bn * 128 bytes)
     SlotLayout slot;       // one K slice of the block's two tile rows
     uint32_t tmem_cols;    // columns of one accumulator (two are allocated)
+    uint64_t reducer_wait_ns;  // how long a row block's first part waits for the others
 };
 
 struct DecompressParams {
@@ -104,6 +105,10 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
                            int max_common, int max_rare, int start_exp, const void* x, void* y,
                            int m, int n, int k, int kparts, const GemmScratch* scratch = nullptr);
 int plan_kparts(int m, int n, int k, int device);
+// How long (ns) the CTA holding a split row block's first K part waits for
+// the other parts before falling back to the last-arrival reduction (both
+// give identical results). Returns the previous value.
+uint64_t set_reducer_wait_ns(uint64_t ns);
 // Scratch the launch needs (both 0 when no CTA range splits a row block).
 void gemm_workspace_bytes(int m, int n, int k, int kparts, int device, size_t* partial_bytes,
                           size_t* counter_bytes);

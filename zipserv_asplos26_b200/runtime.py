@@ -80,6 +80,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "zipserv_mm_plan": (_I, [_I] * 3),
     "zipserv_mm_workspace_size": (_I, [_I] * 4 + [ctypes.POINTER(_U64)] * 2),
     "zipserv_device_flags": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+    "zipserv_mm_reducer_wait": (_U64, [_U64]),
 }
 _CORE = ("zipserv_abi_version", "zipserv_error", "zipserv_compress", "zipserv_free")
 _CUDA_CORE = ("zipserv_mm", "zipserv_decode")
@@ -395,6 +396,13 @@ def plan_kparts(m: int, n: int, k: int) -> int:
     """CTAs per 128-row block of the default schedule on the current GPU
     (at least 1; the persistent grid may also give a CTA several blocks)."""
     return int(_cuda_library().zipserv_mm_plan(m, n, k))
+
+
+def set_reducer_wait(ns: int) -> int:
+    """How long (ns) a split row block's first K part waits for the others
+    before the last-arrival reduction takes over (identical results; 0 sends
+    every split row block that way). Returns the previous value."""
+    return int(_cuda_library().zipserv_mm_reducer_wait(int(ns)))
 
 
 def device_flags(clear: bool = True) -> int:
