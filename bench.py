@@ -383,6 +383,15 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     if world > 1:
         dist.all_reduce(bytes_all)
     step_bytes = float(bytes_all.item())
+    extras = {}
+    if not args.no_extras:
+        # Every rank takes part (the extras' collectives and max-over-ranks).
+        for c in calls:  # free the sweep's device copies (shapes and sizes stay)
+            for key in ("packed", "dense", "x", "out"):
+                c.pop(key, None)
+        torch.cuda.empty_cache()
+        extras["llama70b_tp"] = tp70b_case(args, world, rank, dev)
+        extras["decode_step"] = decode_step_case(args, world, rank, dev)
     if rank != 0:
         return None
     steps = args.steps
@@ -459,6 +468,7 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         "per_shape": per_shape,
     }
     line["clocks"] = sampler.summary()
+    line.update(extras)
     if args.stress and rank == 0:
         line["stress"] = stress_case(args)
     if not args.no_cpu_baseline:
@@ -663,6 +673,125 @@ def run_reference(args, world: int, rank: int) -> dict | None:
     }
 
 
+def decode_step_case(args, world: int, rank: int, dev) -> dict:
+    """one greedy decode step of a random-init
+    Llama-3-8B (32 layers, 2048 cached positions per sequence, untied
+    compressed lm_head) at TP = world, every linear through ZipGEMM, against
+    the same step with the dense BF16 weights (cuBLAS). Each step is a CUDA
+    graph replay (NCCL all-reduces of o and down inside it); the time is the
+    max over ranks of the median of per-replay CUDA events."""
+    import torch
+    import torch.distributed as dist
+
+    from zipserv_asplos26_b200.llama_decode import LLAMA3_8B, DecodeStep
+
+    batches = [b for b in (1, 16, 64) if b <= args.max_step_batch]
+    t0 = time.time()
+    dense = DecodeStep(LLAMA3_8B, max(batches), dev, mode="dense", world=world, rank=rank)
+    zipm = DecodeStep.packed_from(dense)
+    setup_s = time.time() - t0
+    out = {"model": "llama3-8b random init, 32 layers, context 2048, greedy step",
+           "tp": world, "packed_weight_bytes_per_rank": zipm.weight_bytes(),
+           "dense_weight_bytes_per_rank": dense.weight_bytes(),
+           "setup_s": round(setup_s, 1), "batches": []}
+    stream = torch.cuda.Stream(dev)
+    for b in batches:
+        tokens = torch.arange(b, device=dev, dtype=torch.int64) * 977 % 128256
+        row = {"batch": b}
+        for name, model in (("zipgemm", zipm), ("dense_cublas", dense)):
+            graph, nxt = model.capture(tokens, stream)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            times = []
+            for _ in range(max(5, args.steps)):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                graph.replay()
+                e.record()
+                torch.cuda.synchronize(dev)
+                times.append(s.elapsed_time(e))
+            t = torch.tensor([statistics.median(times)], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            row[f"{name}_ms"] = round(float(t.item()), 3)
+            del graph
+        row["tokens_per_s_zipgemm"] = round(b / row["zipgemm_ms"] * 1e3, 1)
+        row["zipgemm_speedup_vs_cublas"] = round(row["dense_cublas_ms"] / row["zipgemm_ms"], 3)
+        out["batches"].append(row)
+    del zipm, dense
+    torch.cuda.empty_cache()
+    return out
+
+
+LLAMA70B = (  # name, M, K, tensor-parallel split (BASELINE configs[3])
+    ("qkv", 10240, 8192, "col"),
+    ("o", 8192, 8192, "row"),
+    ("gate_up", 57344, 8192, "col"),
+    ("down", 8192, 28672, "row"),
+)
+
+
+def tp70b_case(args, world: int, rank: int, dev) -> dict:
+    """the Llama-3-70B linears split over `world` GPUs
+    (qkv and gate_up on output rows, o and down on K), N in {1, 16, 64, 256}.
+    Per call, after a 256 MiB L2 flush: ZipGEMM and cuBLAS BF16 on this
+    rank's shard, and for the row-parallel layers the NCCL all-reduce of the
+    [N, M] BF16 partial output timed separately; max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from zipserv_asplos26_b200 import runtime
+
+    flush = torch.empty(64 * 2**20, dtype=torch.int32, device=dev)
+    rows = []
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        ts = []
+        for _ in range(5):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(dev)
+            ts.append(s.elapsed_time(e) * 1e3)
+        t = torch.tensor([statistics.median(ts)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for li, (name, m, k, split) in enumerate(LLAMA70B):
+        mm, kk, (r0, r1), (c0, c1) = _shard(name, m, k, split, world, rank)
+        g = torch.Generator(device=dev).manual_seed(7000 + li)
+        w = (torch.randn(m, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        local = w[r0:r1, c0:c1].contiguous()
+        del w
+        packed = runtime.compress_device(local)
+        for n in (1, 16, 64, 256):
+            x = torch.randn(n, kk, generator=g, device=dev).to(torch.bfloat16)
+            zus = timed(lambda: runtime.linear(x, packed))
+            dus = timed(lambda: F.linear(x, local))
+            row = {"layer": name, "m": mm, "k": kk, "n": n, "zipgemm_us": round(zus, 2),
+                   "cublas_bf16_us": round(dus, 2),
+                   "gbs": round((packed.storage_bytes + 2 * n * (kk + mm)) / (zus * 1e-6) / 1e9, 1),
+                   "speedup_vs_cublas": round(dus / zus, 3)}
+            if split == "row" and world > 1:
+                y = torch.empty(n, mm, dtype=torch.bfloat16, device=dev)
+                row["allreduce_us"] = round(timed(lambda: dist.all_reduce(y)), 2)
+            rows.append(row)
+        del packed, local
+    flags = runtime.device_flags()
+    if flags:
+        raise SystemExit(f"device failure flags {flags:#x} set during the 70B case")
+    return {"workload": "llama3-70b linears, tp%d shards, N in {1,16,64,256}" % world,
+            "timing": "median of 5 per-call CUDA events after a 256 MiB L2 flush, max over ranks",
+            "per_shape": rows}
+
+
 def stress_case(args) -> dict:
     """BASELINE configs[2] on this GPU: a 28672x8192 weight with 5 % N(0, 1)
     outliers. Standalone decompression (algorithmic bytes = packed + dense
@@ -759,6 +888,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile", metavar="LAYER:N", help="run one linear for ncu, e.g. o:16")
     parser.add_argument("--repeats", type=int, default=4)
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip the Llama-3-70B TP shapes and the Llama-3-8B decode step")
+    parser.add_argument("--max-step-batch", type=int, default=64)
     parser.add_argument("--stress", action="store_true",
                         help="also measure the 28672x8192 outlier-stress weight")
     args = parser.parse_args()

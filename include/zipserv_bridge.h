@@ -150,6 +150,29 @@ int zipserv_mm_plan(int m, int n, int k);
  * previous value. */
 uint64_t zipserv_mm_reducer_wait(uint64_t ns);
 
+/* No counterpart in the reference (its encoder runs on the host only,
+ * csrc/HostPacker.h:95-183): TCA-TBE packing of a BF16 matrix that is already
+ * in device memory, byte-identical to zipserv_compress. Two calls, because the
+ * stream lengths depend on the data:
+ *   1. zipserv_pack_device_plan: `weights` (row-major m x k BF16, 16-byte
+ *      aligned), base = -1 for the most populated 7-exponent window (or a
+ *      fixed window start in [0, 249]); writes the (tiles + 1) offset pairs
+ *      to `global` (device, 16-byte aligned) and uses `scratch` (device,
+ *      zipserv_pack_device_scratch_bytes(), 16-byte aligned). Synchronises
+ *      `stream` and returns in info[0..4]: start_exp, max_common, max_rare and
+ *      the byte lengths of the sm and rare streams.
+ *   2. zipserv_pack_device_encode: writes sm, rare, the three bitmap planes
+ *      and medium (device buffers of the lengths zipserv_compress documents)
+ *      from the same weights, global and scratch, enqueued on `stream`.
+ * Allocates nothing. Returns 0 or a cudaError_t (invalid arguments:
+ * cudaErrorInvalidValue with zipserv_error() set). */
+uint64_t zipserv_pack_device_scratch_bytes(void);
+int zipserv_pack_device_plan(void* stream, const void* weights, int m, int k, int base,
+                             void* global, void* scratch, int32_t* info);
+int zipserv_pack_device_encode(void* stream, const void* weights, int m, int k,
+                               const void* global, const void* scratch, void* sm, void* rare,
+                               void* b1, void* b2, void* b3, void* medium);
+
 /* Device-side failure flags of the current device (bit 0: a pipeline wait
  * in a kernel gave up after its iteration limit; results of that launch are
  * undefined). Reading synchronises the device; clear != 0 resets the flags.

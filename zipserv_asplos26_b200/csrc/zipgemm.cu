@@ -51,6 +51,7 @@
 #include "capi_internal.h"
 #include "codec.h"
 #include "decode.cuh"
+#include "tile_decode.cuh"
 #include "ptx.cuh"
 #include "zipgemm.cuh"
 
@@ -66,6 +67,10 @@ constexpr int gemm_threads(int ndg) { return 256 + 128 * ndg; }
 // segments and arrive long before; the limit only matters when those CTAs
 // could not start (other work holding SMs).
 constexpr uint64_t kReducerWaitNs = 50000;
+// How far ahead (in K-slice steps of a CTA) the producers prefetch weight
+// data into L2 (even, at most 62: the offsets come from the current or the
+// next 32-step chunk of a producer).
+constexpr int kPrefetchSteps = 16;
 
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
@@ -225,8 +230,30 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     ptx::launch_dependents();
     // Prologue, overlapped across warps: warp 0 allocates TMEM while warp 1
     // initialises the barriers (one lane per barrier) and starts the table
-    // copy, and the producers fetch their first step's offsets.
-    int2 first_offs = make_int2(0, 0);
+    // copy, and the producers fetch their first chunk of payload offsets.
+    //
+    // Payload offsets: lane l of producer pi holds, for chunk c, the four
+    // `global` entries (start and end of both tile rows) of its step
+    // pi + 2 * (32c + l); the next chunk is fetched a whole chunk ahead, so
+    // the producers never wait on these global loads.
+    const int2* goffs = reinterpret_cast<const int2*>(p.global);
+    auto fetch_offsets = [&](int pi, int c, int2 (&v)[4]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = make_int2(0, 0);
+        const int s = pi + 2 * (32 * c + lane);
+        if (s < nsteps) {
+            const int item = t_begin + s, unit = item / kt, k = item - unit * kt;
+            const int tr = 2 * (unit % rbs);
+            v[0] = goffs[size_t(tr) * kt + k];
+            v[1] = goffs[size_t(tr) * kt + k + 1];
+            if (tr + 1 < p.row_tiles) {
+                v[2] = goffs[size_t(tr + 1) * kt + k];
+                v[3] = goffs[size_t(tr + 1) * kt + k + 1];
+            }
+        }
+    };
+    int2 first_offs[4];
+    if (warp == 2 || warp == 3) fetch_offsets(warp - 2, 0, first_offs);
     if (warp == 0) {
         ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 2 * p.tmem_cols);
         ptx::tmem_relinquish();
@@ -260,15 +287,6 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             ptx::mbar_arrive_expect_tx(bar_tab, kTableBytes);
             ptx::bulk_g2s(tables, &g_decode_tables, kTableBytes, bar_tab, ptx::policy_evict_last());
         }
-    } else if (warp < 4 && lane < 4) {
-        // Producer pi's first step is pi: lane 2*r + e holds offset entry e of
-        // tile row r of its block.
-        const int pi = warp - 2;
-        int k = t_begin - unit0 * kt + pi, rb = unit0 % rbs;
-        if (k >= kt) k -= kt, rb = rb + 1 == rbs ? 0 : rb + 1;
-        const int tr = 2 * rb + (lane >> 1);
-        if (pi < nsteps && tr < p.row_tiles)
-            first_offs = reinterpret_cast<const int2*>(p.global)[size_t(tr) * kt + k + (lane & 1)];
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -366,7 +384,6 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         // payload run, all completing on the slot's barrier. The packed
         // weight is never written by other kernels: no prerequisite wait.
         const int pi = warp - 2;
-        const int2* goffs = reinterpret_cast<const int2*>(p.global);
         const uint64_t pol_w = ptx::policy_evict_first();
         // Position (K slice, row block) of a step, advanced without divisions.
         struct Pos {
@@ -379,30 +396,43 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 if (++q.rb == rbs) q.rb = 0;
             }
         };
-        // Lanes 0-3 hold the (common, rare) offsets of a step: lane 2*r + e
-        // = entry e (0 start, 1 end) of tile row r of the step's block.
-        auto load_offsets = [&](int t, const Pos& q) {
-            int2 v = make_int2(0, 0);
-            if (t < nsteps && lane < 4) {
-                const int tr = 2 * q.rb + (lane >> 1);
-                if (tr < p.row_tiles) v = goffs[size_t(tr) * kt + q.k + (lane & 1)];
-            }
-            return v;
-        };
         Pos cur{t_begin - unit0 * kt, unit0 % rbs};
         advance(cur, pi);
-        Pos nxt = cur;
-        advance(nxt, 2);
-        int2 o = first_offs;  // load_offsets(pi, cur), fetched before the CTA sync
+        // The step kPrefetchSteps ahead of the one being filled is prefetched
+        // into L2, so a slot's copies read L2 rather than DRAM: with two
+        // slots per decoder group, a fill must land within about one step
+        // of decoding, shorter than a DRAM round trip under load.
+        Pos pf = cur;
+        advance(pf, kPrefetchSteps);
+        int2 chunk[4], ahead[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) chunk[i] = first_offs[i];
         bool ok = true;
         int last = -1;  // last step issued
-        for (int t = pi, u = pi / NDG, g = pi % NDG; t < nsteps; t += 2) {
-            const int2 onext = load_offsets(t + 2, nxt);
-            const int sidx = g * 2 + (u & 1);
-            int2 e[4];
+        for (int t = pi, i = 0, u = pi / NDG, g = pi % NDG; t < nsteps; t += 2, ++i) {
+            const int ci = i & 31;
+            if (ci == 0) {
+                if (i > 0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                e[i].x = __shfl_sync(kFullMask, o.x, i), e[i].y = __shfl_sync(kFullMask, o.y, i);
+                    for (int j = 0; j < 4; ++j) chunk[j] = ahead[j];
+                }
+                fetch_offsets(pi, (i >> 5) + 1, ahead);
+            }
+            const int sidx = g * 2 + (u & 1);
+            int2 e[4], f[4];
+            // Entries of the step kPrefetchSteps ahead: lane ci + kPrefetchSteps / 2
+            // of this chunk or of the next one.
+            const int fi = ci + kPrefetchSteps / 2;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                e[j].x = __shfl_sync(kFullMask, chunk[j].x, ci);
+                e[j].y = __shfl_sync(kFullMask, chunk[j].y, ci);
+                const int ax = __shfl_sync(kFullMask, chunk[j].x, fi & 31);
+                const int ay = __shfl_sync(kFullMask, chunk[j].y, fi & 31);
+                const int bx = __shfl_sync(kFullMask, ahead[j].x, fi & 31);
+                const int by = __shfl_sync(kFullMask, ahead[j].y, fi & 31);
+                f[j] = fi < 32 ? make_int2(ax, ay) : make_int2(bx, by);
+            }
             if (lane == 0) {
                 if (u >= 2) ok = ptx::mbar_wait(bar_addr(bar_free, sidx), ((u >> 1) - 1) & 1);
                 if (ok) {
@@ -441,11 +471,31 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                     if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[2].y, rlen[1], full, pol_w);
                     last = t;
                 }
+                if (ok && t + kPrefetchSteps < nsteps) {
+                    const bool has1 = 2 * pf.rb + 1 < p.row_tiles;
+                    if (pm.count == 1) ptx::tma_prefetch_4d(&pm.map[0], 0, pf.k, 2 * pf.rb, 0);
+                    else
+                        for (int i = 0; i < 3; ++i)
+                            ptx::tma_prefetch_3d(&pm.map[i], 0, pf.k, 2 * pf.rb);
+                    ptx::tma_prefetch_3d(&mmap, 0, pf.k, 2 * pf.rb);
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const int2 st = f[2 * r], en = f[2 * r + 1];
+                        if (r == 1 && !has1) break;
+                        const uint32_t cl = (st.x & 15) == 0
+                                                ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
+                                                : 0u;
+                        const uint32_t rl = (st.y & 7) == 0
+                                                ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
+                                                : 0u;
+                        if (cl) ptx::bulk_prefetch_l2(p.sm + st.x, cl);
+                        if (rl) ptx::bulk_prefetch_l2(p.rare + st.y, rl);
+                    }
+                }
             }
             if (!__shfl_sync(kFullMask, ok, 0)) break;
-            o = onext;
-            cur = nxt;
-            advance(nxt, 2);
+            advance(cur, 2);
+            advance(pf, 2);
             if ((g += 2) >= NDG) g -= NDG, ++u;
         }
         // Never leave copies in flight: wait (bounded) for the last use of
@@ -461,13 +511,9 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         const int dw = warp - 4, g = dw >> 2;
         const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
         const int tau = lane >> 4;
-        RowDecoder dec;
+        TileDecoder dec;
         dec.init(tables, lane, q, p.start_exp);
-        // This thread's row of the group's A tile: MMA row m = 32*q + lane
-        // (= accumulator lane), 128-byte swizzled.
-        const uint32_t mr = uint32_t(32 * q + lane);
-        const uint32_t arow = sbase + p.off_a + (mr >> 3) * 1024u + (mr & 7u) * 128u;
-        const uint32_t swz = (mr & 7u) << 4;
+        const uint32_t abase = sbase + p.off_a;
         const int na = p.na;  // >= NDG
         bool ok = ptx::mbar_wait(bar_tab, 0);
 
@@ -483,21 +529,13 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             const int sidx = g * 2 + (u & 1);
             const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
             ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), (u >> 1) & 1);
-            if (!__all_sync(kFullMask, ok)) break;
-            uint32_t out[32];
-            RareState rs;
-            dec.decode(slot + uint32_t(tau) * L.plane1, L.plane_stride,
-                       slot + L.med + uint32_t(tau) * 32u, slot + (tau ? L.common1 : L.common0),
-                       cap_c, cap_r, out, rs);
-            if (__any_sync(kFullMask, !valid)) {  // only in a ragged last row block
-#pragma unroll
-                for (int w = 0; w < 32; ++w) out[w] = valid ? out[w] : 0u;
-            }
             // A tile a = t % na is free once the MMAs of step t - na finished.
-            if (ause > 0) ok = ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
+            if (ause > 0) ok = ok && ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
-            dec.store(arow + uint32_t(a) * kATileBytes, swz, out, rs,
-                      slot + (tau ? L.rare1 : L.rare0), cap_r, !valid);
+            dec.decode_store(slot + uint32_t(tau) * L.plane1, L.plane_stride,
+                             slot + L.med + uint32_t(tau) * 32u,
+                             slot + (tau ? L.common1 : L.common0), slot + (tau ? L.rare1 : L.rare0),
+                             cap_c, cap_r, abase + uint32_t(a) * kATileBytes, valid);
             // Generic-proxy stores must be visible to the tensor cores.
             ptx::fence_proxy_async_smem();
             __syncwarp();

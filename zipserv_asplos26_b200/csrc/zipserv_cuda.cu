@@ -4,3 +4,4 @@
 #include "decompress.cu"
 #include "capi_cuda.cu"
 #include "noalloc.cu"
+#include "gpu_packer.cu"

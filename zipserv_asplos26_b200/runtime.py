@@ -81,6 +81,9 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "zipserv_mm_workspace_size": (_I, [_I] * 4 + [ctypes.POINTER(_U64)] * 2),
     "zipserv_device_flags": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
     "zipserv_mm_reducer_wait": (_U64, [_U64]),
+    "zipserv_pack_device_scratch_bytes": (_U64, []),
+    "zipserv_pack_device_plan": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ctypes.c_int32)]),
+    "zipserv_pack_device_encode": (_I, [_P, _P, _I, _I, _P, _P] + [_P] * 6),
 }
 _CORE = ("zipserv_abi_version", "zipserv_error", "zipserv_compress", "zipserv_free")
 _CUDA_CORE = ("zipserv_mm", "zipserv_decode")
@@ -251,6 +254,44 @@ def compress(weight: Tensor) -> PackedWeight:
     finally:
         _release(lib, descriptor)
     return PackedWeight(views, *meta, arena)
+
+
+def compress_device(weight: Tensor, base: int = -1) -> PackedWeight:
+    """Pack a BF16 matrix that is already on a GPU, on that GPU, into an
+    arena there; the bytes equal ``compress(weight.cpu())`` exactly. The
+    weight is read on the current stream; the call waits once for the stream
+    lengths (they depend on the data). ``base`` fixes the 7-exponent window's
+    first exponent (0..249) instead of choosing the most populated one."""
+    if type(base) is not int or not -1 <= base <= 249:
+        raise ValueError("base must be -1 or an exponent in [0, 249]")
+    if weight.device.type != "cuda" or weight.dtype != torch.bfloat16 or weight.ndim != 2:
+        raise ValueError("ZipServ device compression requires a two-dimensional CUDA BF16 tensor")
+    m, k = weight.shape
+    if m <= 0 or k <= 0 or m % 64 or k % 64 or m * k > 2**31 - 4097:
+        raise ValueError("ZipServ requires positive, 64-aligned dimensions and int32 offsets")
+    lib = _cuda_library()
+    if not hasattr(lib, "zipserv_pack_device_plan"):
+        raise RuntimeError("This ZipServ library has no device packer")
+    device = weight.device
+    with torch.cuda.device(device):
+        source = weight.contiguous()
+        tiles = (m // 64) * (k // 64)
+        offsets = torch.empty((tiles + 1) * 8, dtype=torch.uint8, device=device)
+        scratch = torch.empty(int(lib.zipserv_pack_device_scratch_bytes()), dtype=torch.uint8,
+                              device=device)
+        info = (ctypes.c_int32 * 5)()
+        stream = _stream(device)
+        _check(lib.zipserv_pack_device_plan(stream, source.data_ptr(), m, k, base,
+                                            offsets.data_ptr(), scratch.data_ptr(), info))
+        start_exp, max_common, max_rare, sm_bytes, rare_bytes = (int(v) for v in info)
+        lengths = [sm_bytes, rare_bytes, tiles * 512, tiles * 512, tiles * 512, tiles * 32,
+                   (tiles + 1) * 8]
+        arena, views = _new_arena(lengths, device)
+        views[6].copy_(offsets)
+        _check(lib.zipserv_pack_device_encode(stream, source.data_ptr(), m, k,
+                                              views[6].data_ptr(), scratch.data_ptr(),
+                                              *(v.data_ptr() for v in views[:6])))
+    return PackedWeight(views, m, k, max_common, max_rare, start_exp, arena)
 
 
 # ---------------------------------------------------------------- forward
