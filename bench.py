@@ -229,7 +229,21 @@ def run_ours(args, world: int, rank: int) -> dict | None:
 
     total_bytes = sum(call_bytes(c) for c in calls)
 
+    # Row-parallel layers sum their outputs across ranks inside the fused
+    # kernel (tp.PeerExchange); the NCCL all-reduce variant is timed beside it.
+    exchange = None
+    if need_reduce:
+        from zipserv_asplos26_b200 import tp as tpmod
+
+        exchange = tpmod.PeerExchange(max(l["m"] for l in layers if l["split"] == "row"),
+                                      max(args.tokens), device=dev)
+
     def zip_call(c):
+        if need_reduce and c["lay"]["split"] == "row":
+            return exchange.linear(c["x"], c["packed"], out=c["out"])
+        return runtime.linear_kparts(c["x"], c["packed"], 0, out=c["out"])
+
+    def zip_nccl_call(c):
         y = runtime.linear_kparts(c["x"], c["packed"], 0, out=c["out"])
         if need_reduce and c["lay"]["split"] == "row":
             dist.all_reduce(y)
@@ -299,9 +313,12 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     barrier()
     per_call: dict = {}
     dense_per_call: dict = {}
+    nccl_per_call: dict = {}
     for _ in range(max(3, min(args.steps, 10))):
         per_call_pass(zip_call, per_call)
         per_call_pass(dense_call, dense_per_call)
+        if need_reduce:
+            per_call_pass(zip_nccl_call, nccl_per_call)
     barrier()
     ref_gpu, ref_gpu_note = (_reference_gpu_per_call(calls, stream, dev, settle)
                              if world == 1 else ({}, "single-GPU runs only"))
@@ -338,9 +355,10 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         for i, c in enumerate(calls):
             if i % group == 0:  # this group's inputs are on the device
                 stream.wait_event(landed[min(len(calls), i + group) - 1])
-            y = runtime.linear(dev_x[i], c["packed"])
             if need_reduce and c["lay"]["split"] == "row":
-                dist.all_reduce(y)
+                y = exchange.linear(dev_x[i], c["packed"])
+            else:
+                y = runtime.linear(dev_x[i], c["packed"])
             pending.append((i, y))
             if len(pending) == group or i == len(calls) - 1:
                 done = torch.cuda.Event()
@@ -384,6 +402,8 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         dist.all_reduce(bytes_all)
     step_bytes = float(bytes_all.item())
     extras = {}
+    if exchange is not None:
+        exchange.close()
     if not args.no_extras:
         # Every rank takes part (the extras' collectives and max-over-ranks).
         for c in calls:  # free the sweep's device copies (shapes and sizes stay)
@@ -408,6 +428,9 @@ def run_ours(args, world: int, rank: int) -> dict | None:
                "zipgemm_us": round(us, 2), "cublas_bf16_us": round(dus, 2),
                "gbs": round(call_bytes(c) / (us * 1e-6) / 1e9, 1),
                "speedup_vs_cublas": round(dus / us, 3)}
+        if key in nccl_per_call:
+            row["zipgemm_then_nccl_allreduce_us"] = round(
+                statistics.median(nccl_per_call[key]) * 1e3, 2)
         if key in ref_gpu:
             rus, rsplit = ref_gpu[key]
             row.update({"reference_gpu_us": round(rus, 2), "reference_split_k": rsplit,
@@ -688,9 +711,17 @@ def decode_step_case(args, world: int, rank: int, dev) -> dict:
     batches = [b for b in (1, 16, 64) if b <= args.max_step_batch]
     t0 = time.time()
     dense = DecodeStep(LLAMA3_8B, max(batches), dev, mode="dense", world=world, rank=rank)
-    zipm = DecodeStep.packed_from(dense)
+    exchange = None
+    if world > 1:
+        from zipserv_asplos26_b200 import tp as tpmod
+
+        exchange = tpmod.PeerExchange(LLAMA3_8B.hidden, max(batches), device=dev)
+    zipm = DecodeStep.packed_from(dense, exchange=exchange)
     setup_s = time.time() - t0
     out = {"model": "llama3-8b random init, 32 layers, context 2048, greedy step",
+           "row_parallel_reduction": ("fused in the ZipGEMM kernel (peer stores over NVLink); "
+                                      "dense cuBLAS arm uses an NCCL all-reduce")
+           if world > 1 else "none (one GPU)",
            "tp": world, "packed_weight_bytes_per_rank": zipm.weight_bytes(),
            "dense_weight_bytes_per_rank": dense.weight_bytes(),
            "setup_s": round(setup_s, 1), "batches": []}
@@ -720,6 +751,8 @@ def decode_step_case(args, world: int, rank: int, dev) -> dict:
         row["zipgemm_speedup_vs_cublas"] = round(row["dense_cublas_ms"] / row["zipgemm_ms"], 3)
         out["batches"].append(row)
     del zipm, dense
+    if exchange is not None:
+        exchange.close()
     torch.cuda.empty_cache()
     return out
 
@@ -746,6 +779,11 @@ def tp70b_case(args, world: int, rank: int, dev) -> dict:
 
     flush = torch.empty(64 * 2**20, dtype=torch.int32, device=dev)
     rows = []
+    exchange = None
+    if world > 1:
+        from zipserv_asplos26_b200 import tp as tpmod
+
+        exchange = tpmod.PeerExchange(8192, 256, device=dev)
 
     def timed(fn):
         for _ in range(2):
@@ -781,15 +819,66 @@ def tp70b_case(args, world: int, rank: int, dev) -> dict:
                    "speedup_vs_cublas": round(dus / zus, 3)}
             if split == "row" and world > 1:
                 y = torch.empty(n, mm, dtype=torch.bfloat16, device=dev)
-                row["allreduce_us"] = round(timed(lambda: dist.all_reduce(y)), 2)
+                row["nccl_allreduce_us"] = round(timed(lambda: dist.all_reduce(y)), 2)
+                row["zipgemm_fused_allreduce_us"] = round(
+                    timed(lambda: exchange.linear(x, packed, out=y)), 2)
             rows.append(row)
         del packed, local
+    if exchange is not None:
+        exchange.close()
     flags = runtime.device_flags()
     if flags:
         raise SystemExit(f"device failure flags {flags:#x} set during the 70B case")
     return {"workload": "llama3-70b linears, tp%d shards, N in {1,16,64,256}" % world,
             "timing": "median of 5 per-call CUDA events after a 256 MiB L2 flush, max over ranks",
             "per_shape": rows}
+
+
+def threshold_sweep(args) -> None:
+    """Per-shape crossover between the fused kernel and decompression + cuBLAS
+    BF16 (the planner's large-batch route), one B200, per-call CUDA events
+    after a 256 MiB L2 flush. Prints one JSON line."""
+    import torch
+    import torch.nn.functional as F
+
+    from zipserv_asplos26_b200 import runtime
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(64 * 2**20, dtype=torch.int32, device=dev)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        ts = []
+        for _ in range(7):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(dev)
+            ts.append(s.elapsed_time(e) * 1e3)
+        return statistics.median(ts)
+
+    out = []
+    for li, (name, m, k, _split) in enumerate(LAYERS + LLAMA70B):
+        g = torch.Generator(device=dev).manual_seed(9000 + li)
+        w = (torch.randn(m, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        packed = runtime.compress_device(w)
+        dense = torch.empty_like(w)
+        row = {"layer": name, "m": m, "k": k, "points": []}
+        cross = None
+        for n in (16, 32, 64, 96, 128, 192, 256, 384, 512, 768):
+            x = torch.randn(n, k, generator=g, device=dev).to(torch.bfloat16)
+            fused = timed(lambda: runtime.linear(x, packed))
+            route = timed(lambda: F.linear(x, runtime.decompress(packed, out=dense)))
+            row["points"].append([n, round(fused, 1), round(route, 1)])
+            if cross is None and route < fused:
+                cross = n
+        row["first_n_where_decode_route_wins"] = cross
+        out.append(row)
+        del w, packed, dense
+    print(json.dumps({"threshold_sweep": out}), flush=True)
 
 
 def stress_case(args) -> dict:
@@ -891,11 +980,16 @@ def main() -> None:
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the Llama-3-70B TP shapes and the Llama-3-8B decode step")
     parser.add_argument("--max-step-batch", type=int, default=64)
+    parser.add_argument("--threshold-sweep", action="store_true",
+                        help="measure the fused vs decompress + cuBLAS crossover per shape")
     parser.add_argument("--stress", action="store_true",
                         help="also measure the 28672x8192 outlier-stress weight")
     args = parser.parse_args()
     if args.profile:
         run_profile_case(args.profile, args.repeats)
+        return
+    if args.threshold_sweep:
+        threshold_sweep(args)
         return
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))

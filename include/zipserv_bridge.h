@@ -173,6 +173,41 @@ int zipserv_pack_device_encode(void* stream, const void* weights, int m, int k,
                                const void* global, const void* scratch, void* sm, void* rare,
                                void* b1, void* b2, void* b3, void* medium);
 
+/* No counterpart in the reference (row-parallel layers leave their
+ * all-reduce to vLLM/NCCL): the fused GEMM of a row-parallel shard with the
+ * all-reduce of its output across `world` GPUs (2..8) in the same kernel.
+ * Each rank passes its K shard of W and x; every rank receives the full
+ * y = sum over ranks. When a CTA holds the final FP32 value of a 32-row x
+ * bn-column piece it stores it into every rank's receive buffer (peer
+ * stores over NVLink), raises its flag on every rank, waits (bounded) for
+ * the other ranks' flags, sums the ranks' values in rank order (so every
+ * rank stores identical BF16 outputs) and stores y. recv[r] / flags[r] are
+ * rank r's receive buffer and flag array as this process maps them (its own
+ * at index rank; the others opened through zipserv_ipc_open), each at least
+ * the sizes zipserv_mm_allreduce_sizes reports and zero-filled before first
+ * use; `state` is this rank's 16-byte, zero-filled launch counter, advanced
+ * by the kernel (so CUDA graphs may capture the call). Every rank must make
+ * the same sequence of calls with the same shapes; a rank that does not
+ * arrive makes the others give up after about 2 s (device flag bit 0).
+ * No TMA or bulk copy reads another GPU's memory. */
+int zipserv_mm_allreduce_sizes(int m, int n, int world, uint64_t* recv_bytes,
+                               uint64_t* flag_bytes);
+int zipserv_mm_allreduce(void* stream, const void* sm, const void* rare, const void* b1,
+                         const void* b2, const void* b3, const void* medium, const void* global,
+                         int max_common, int max_rare, int start_exp, const void* x, void* y,
+                         int m, int n, int k, int world, int rank, void* const* recv,
+                         void* const* flags, void* state, uint64_t recv_bytes,
+                         uint64_t flag_bytes);
+/* Device memory shared between ranks through CUDA IPC: zipserv_ipc_alloc
+ * returns zero-filled memory, zipserv_ipc_handle writes its 64-byte handle,
+ * zipserv_ipc_open maps another process's handle (peer access enabled),
+ * zipserv_ipc_close / zipserv_ipc_free release them. */
+int zipserv_ipc_alloc(uint64_t bytes, void** ptr);
+int zipserv_ipc_free(void* ptr);
+int zipserv_ipc_handle(void* ptr, void* handle);
+int zipserv_ipc_open(const void* handle, void** ptr);
+int zipserv_ipc_close(void* ptr);
+
 /* Device-side failure flags of the current device (bit 0: a pipeline wait
  * in a kernel gave up after its iteration limit; results of that launch are
  * undefined). Reading synchronises the device; clear != 0 resets the flags.

@@ -144,3 +144,21 @@ def test_l_api_header_declares_reference_entry_points():
     for name in ("BF16TripleBitmap_MM_API", "BF16TripleBitmap_MM_API_FP32",
                  "BF16TripleBitmap_Decompress_API", "InitBF16MatrixTripleBitmap"):
         assert re.search(rf"\b{name}\s*\(", text), name
+
+
+def test_fused_allreduce_sizes_and_argument_checks(native_lib):
+    """zipserv_mm_allreduce_sizes: receive buffer = 2 parities x world x the
+    [N tile x 128] FP32 pieces of every unit; flags = 2 x world x units x 4
+    quarters. Invalid worlds and exchanges are refused before any GPU work."""
+    rb, fb = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 2, ctypes.byref(rb), ctypes.byref(fb)) == 0
+    units = 4096 // 128
+    assert rb.value == 2 * 2 * units * 16 * 128 * 4
+    assert fb.value == 2 * 2 * units * 4 * 4
+    assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 1, ctypes.byref(rb), ctypes.byref(fb)) == 1
+    assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 9, ctypes.byref(rb), ctypes.byref(fb)) == 1
+    bufs = [None] * 7
+    for world, rank in ((1, 0), (9, 0), (2, 2), (2, -1)):
+        assert native_lib.zipserv_mm_allreduce(None, *bufs, 4048, 120, 115, None, None, 4096, 16,
+                                               4096, world, rank, None, None, None, 0, 0) == 1
+        assert b"world" in native_lib.zipserv_error()

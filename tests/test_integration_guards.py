@@ -42,6 +42,26 @@ def test_startup_and_decode_budget_rejections():
     assert policy.decode_budget_rejection(4096, 4096, policy.DispatchSettings()) is None
 
 
+def test_per_shape_threshold():
+    """with per_shape_threshold each layer is also capped at its
+    measured B200 crossover, smaller weights switching to decompression +
+    stock GEMM at fewer tokens."""
+    limits = [policy.b200_token_limit(m, k) for m, k in
+              ((4096, 4096), (6144, 4096), (4096, 14336), (28672, 4096), (57344, 8192))]
+    assert limits == sorted(limits) and all(v >= 1 for v in limits)
+    on = policy.DispatchSettings(mode="shape", per_shape_threshold=True)
+    off = policy.DispatchSettings(mode="shape")
+    small, large = (4096, 4096), (28672, 4096)
+    n = policy.b200_token_limit(*small) + 1
+    assert policy.select_split(*small[:1], n, small[1], 148, on) is None
+    assert policy.select_split(*small[:1], n, small[1], 148, off) is not None
+    assert policy.fused_token_limit(*large, on) == min(768, policy.b200_token_limit(*large))
+    capped = policy.DispatchSettings(mode="shape", per_shape_threshold=True, large_batch_tokens=8)
+    assert policy.fused_token_limit(*large, capped) == 8
+    with pytest.raises(ValueError):
+        policy.DispatchSettings(per_shape_threshold=1)
+
+
 @pytest.mark.parametrize("bad", [dict(mode="auto"), dict(partial_dtype="fp16"),
                                  dict(large_batch_tokens=0), dict(workspace_bytes=-1),
                                  dict(decode_workspace_bytes=1.5)])

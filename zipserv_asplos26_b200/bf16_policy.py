@@ -38,6 +38,27 @@ STARTUP_SLICES = 3.0      # per-CTA fixed cost, in K-slice units (B200 measureme
 # CUDA-graph capture sizes within it.
 B200_LARGE_BATCH_TOKENS = 176
 
+# Per-weight crossover on a B200: the first token count at which
+# decompression + cuBLAS BF16 beats the fused kernel, per weight size (M*K
+# elements), measured with per-call device time after an L2 flush
+# (bench.py --threshold-sweep). A weight above the last bound uses its value.
+B200_CROSSOVER = (
+    (20_000_000, 64),
+    (40_000_000, 96),
+    (80_000_000, 192),
+    (float("inf"), 320),
+)
+
+
+def b200_token_limit(m: int, k: int) -> int:
+    """Largest token count the fused kernel should serve for an m x k weight
+    on a B200 (one below the measured crossover)."""
+    elements = m * k
+    for bound, crossover in B200_CROSSOVER:
+        if elements <= bound:
+            return crossover - 1
+    return B200_CROSSOVER[-1][1] - 1
+
 
 @dataclass(frozen=True)
 class DispatchSettings:
@@ -53,6 +74,10 @@ class DispatchSettings:
     workspace_bytes: int = 64 * 2**20
     partial_dtype: str = "bf16"
     decode_workspace_bytes: int = 256 * 2**20
+    # Also cap each layer at its measured B200 crossover (b200_token_limit),
+    # so small layers switch to decompression + stock GEMM sooner than large
+    # ones.
+    per_shape_threshold: bool = False
 
     def __post_init__(self):
         if self.mode not in ("fixed", "tokens", "shape"):
@@ -63,6 +88,8 @@ class DispatchSettings:
             value = getattr(self, name)
             if type(value) is not int or value < 1:
                 raise ValueError(f"{name} must be a positive integer")
+        if type(self.per_shape_threshold) is not bool:
+            raise ValueError("per_shape_threshold must be true or false")
         for name in ("workspace_bytes", "decode_workspace_bytes"):
             value = getattr(self, name)
             if type(value) is not int or value < 0:
@@ -149,13 +176,20 @@ def split_candidates(m: int, tokens: int, k: int, sms: int, workspace_bytes: int
     return tuple(out)
 
 
+def fused_token_limit(m: int, k: int, settings: DispatchSettings) -> int:
+    """Largest batch the planner sends to the fused kernel for an m x k weight."""
+    if settings.per_shape_threshold:
+        return min(settings.large_batch_tokens, b200_token_limit(m, k))
+    return settings.large_batch_tokens
+
+
 @lru_cache(maxsize=4096)
 def select_split(m: int, tokens: int, k: int, sms: int, settings: DispatchSettings,
                  fixed_split: int = 1) -> int | None:
     """The split to request, or None for decode + stock GEMM (large batches)."""
     if settings.mode == "fixed":
         return fixed_split
-    if tokens > settings.large_batch_tokens:
+    if tokens > fused_token_limit(m, k, settings):
         return None
     candidates = split_candidates(m, tokens, k, sms, settings.workspace_bytes,
                                   4 if settings.partial_dtype == "fp32" else 2)

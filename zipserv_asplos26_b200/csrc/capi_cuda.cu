@@ -9,6 +9,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 
 #include "../../include/zipserv_bridge.h"
 #include "capi_internal.h"
@@ -30,7 +31,8 @@ cudaError_t mm_impl(cudaStream_t stream, const void* sm, const void* rare, const
                     const void* b2, const void* b3, const void* medium, const void* global,
                     int max_common, int max_rare, int start_exp, const void* x, void* y, int m,
                     int n, int k, const void* workspace, int split_k, int kparts,
-                    const zs::GemmScratch* scratch = nullptr) {
+                    const zs::GemmScratch* scratch = nullptr,
+                    const zs::TpExchange* tp = nullptr) {
     if (!zs::valid_gemm(m, n, k, split_k) || !zs::valid_counts(max_common, max_rare))
         return fail(cudaErrorInvalidValue,
                     "invalid GEMM shape, Split-K or packed maxima (M, K multiples of 64; "
@@ -44,7 +46,7 @@ cudaError_t mm_impl(cudaStream_t stream, const void* sm, const void* rare, const
         (rare && !aligned16(rare)))
         return fail(cudaErrorInvalidValue, "device buffers must be 16-byte aligned");
     return zs::launch_zipgemm(stream, sm, rare, b1, b2, b3, medium, global, max_common,
-                              max_rare, start_exp, x, y, m, n, k, kparts, scratch);
+                              max_rare, start_exp, x, y, m, n, k, kparts, scratch, tp);
 }
 
 cudaError_t decode_impl(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
@@ -194,6 +196,78 @@ extern "C" int zipserv_mm_plan(int m, int n, int k) {
 }
 
 extern "C" uint64_t zipserv_mm_reducer_wait(uint64_t ns) { return zs::set_reducer_wait_ns(ns); }
+
+// ------------------------------------------------ fused row-parallel all-reduce
+
+extern "C" int zipserv_mm_allreduce_sizes(int m, int n, int world, uint64_t* recv_bytes,
+                                          uint64_t* flag_bytes) {
+    if (!recv_bytes || !flag_bytes) return int(cudaErrorInvalidValue);
+    size_t r = 0, f = 0;
+    zs::allreduce_exchange_bytes(m, n, world, &r, &f);
+    *recv_bytes = r, *flag_bytes = f;
+    if (!r) {
+        zs_set_error("zipserv_mm_allreduce_sizes: invalid M, N or world (2..8)");
+        return int(cudaErrorInvalidValue);
+    }
+    return 0;
+}
+
+extern "C" int zipserv_mm_allreduce(void* stream, const void* sm, const void* rare,
+                                    const void* b1, const void* b2, const void* b3,
+                                    const void* medium, const void* global, int max_common,
+                                    int max_rare, int start_exp, const void* x, void* y, int m,
+                                    int n, int k, int world, int rank, void* const* recv,
+                                    void* const* flags, void* state, uint64_t recv_bytes,
+                                    uint64_t flag_bytes) {
+    if (world < 2 || world > zs::kMaxTp || rank < 0 || rank >= world || !recv || !flags ||
+        !state || !aligned16(state)) {
+        zs_set_error("zipserv_mm_allreduce: world must be 2..8, rank in [0, world), exchange "
+                     "pointers non-null (state 16-byte aligned)");
+        return int(cudaErrorInvalidValue);
+    }
+    if (n > 0 && zs::valid_gemm(m, n, k, 1)) {
+        size_t need_r = 0, need_f = 0;
+        zs::allreduce_exchange_bytes(m, n, world, &need_r, &need_f);
+        if (recv_bytes < need_r || flag_bytes < need_f) {
+            zs_set_error("zipserv_mm_allreduce: receive buffer or flags smaller than "
+                         "zipserv_mm_allreduce_sizes reports");
+            return int(cudaErrorInvalidValue);
+        }
+        for (int r = 0; r < world; ++r)
+            if (!recv[r] || !flags[r] || !aligned16(recv[r]) || !aligned16(flags[r])) {
+                zs_set_error("zipserv_mm_allreduce: every rank's buffers must be non-null and "
+                             "16-byte aligned");
+                return int(cudaErrorInvalidValue);
+            }
+    }
+    const zs::TpExchange tp{world, rank, recv, flags, state};
+    return int(mm_impl(static_cast<cudaStream_t>(stream), sm, rare, b1, b2, b3, medium, global,
+                       max_common, max_rare, start_exp & 255, x, y, m, n, k, nullptr, 1, 0,
+                       nullptr, &tp));
+}
+
+// Device memory a process shares with the other ranks through CUDA IPC.
+extern "C" int zipserv_ipc_alloc(uint64_t bytes, void** ptr) {
+    if (!ptr || !bytes) return int(cudaErrorInvalidValue);
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+    if (e != cudaSuccess) zs_set_error(cudaGetErrorString(e));
+    return int(e);
+}
+extern "C" int zipserv_ipc_free(void* ptr) { return int(cudaFree(ptr)); }
+extern "C" int zipserv_ipc_handle(void* ptr, void* handle) {
+    if (!ptr || !handle) return int(cudaErrorInvalidValue);
+    return int(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), ptr));
+}
+extern "C" int zipserv_ipc_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return int(cudaErrorInvalidValue);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) zs_set_error(cudaGetErrorString(e));
+    return int(e);
+}
+extern "C" int zipserv_ipc_close(void* ptr) { return int(cudaIpcCloseMemHandle(ptr)); }
 
 extern "C" int zipserv_device_flags(unsigned* flags, int clear) {
     if (!flags) return int(cudaErrorInvalidValue);

@@ -37,7 +37,10 @@
 namespace zs {
 
 constexpr uint32_t kFullMask = 0xFFFFFFFFu;
-constexpr int kCodeTableBytes = 256 * 32 * 4;  // per bitmap byte x per lane
+// The code table is replicated kTableCopies times (lane l reads copy l % 32):
+// a warp's lookups never meet bank conflicts.
+constexpr int kTableCopies = 32;
+constexpr int kCodeTableBytes = 256 * kTableCopies * 4;  // per bitmap byte x per copy
 constexpr int kTableBytes = kCodeTableBytes;
 // Bytes of readable shared memory required after the slot ring: payload
 // reads are not clamped per row segment and may run past a corrupted tile.
@@ -45,9 +48,9 @@ constexpr int kRingPadBytes = 2048;
 
 // ------------------------------------------------------- lookup tables
 struct DecodeTables {
-    // Code table: bit p of a bitmap byte -> bit 0 of nibble p, replicated per
-    // lane (entry m of lane l at [m][l]).
-    uint32_t code[256][32];
+    // Code table: bit p of a bitmap byte -> bit 0 of nibble p, replicated
+    // (entry m of copy c at [m][c]).
+    uint32_t code[256][kTableCopies];
 };
 
 __host__ __device__ constexpr DecodeTables make_decode_tables() {
@@ -55,7 +58,7 @@ __host__ __device__ constexpr DecodeTables make_decode_tables() {
     for (int m = 0; m < 256; ++m) {
         uint32_t v = 0;
         for (int p = 0; p < 8; ++p) v |= uint32_t((m >> p) & 1) << (4 * p);
-        for (int l = 0; l < 32; ++l) t.code[m][l] = v;
+        for (int l = 0; l < kTableCopies; ++l) t.code[m][l] = v;
     }
     return t;
 }
@@ -89,14 +92,14 @@ struct RowDecoder {
     uint32_t xp_lo, xp_hi;
     // Multipliers kept in registers so address and selector arithmetic runs
     // as IMAD on the FMA pipe instead of shifts on the integer ALU pipe.
-    uint32_t kone, k2, k4, k8, k128, krank, khi;
+    uint32_t kone, k2, k4, k8, kent, krank, khi;
 
     // The warp decodes band `band_` of both tiles; lane = tau*16 + rt*8 + r.
     __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int band_,
                                          uint32_t start_exp) {
         const int r = lane & 7, rt = (lane >> 3) & 1;
         band = band_;
-        ct = tables_smem + uint32_t(lane) * 4u;
+        ct = tables_smem + uint32_t(lane % kTableCopies) * 4u;
         // Small tile (band, j, rt) is bitmap word pair band*16 + 2j + rt; byte r is row r.
         bm_byte = uint32_t((band * 16 + rt) * 8 + r);
         lane16 = uint32_t(lane) & 15u;
@@ -111,7 +114,7 @@ struct RowDecoder {
         k2 = ptx::launder(2u);
         k4 = ptx::launder(4u);
         k8 = ptx::launder(8u);
-        k128 = ptx::launder(128u);
+        kent = ptx::launder(uint32_t(kTableCopies) * 4u);
         krank = ptx::launder(0x11111110u);
         khi = ptx::launder(0x10000u);
     }
@@ -137,9 +140,9 @@ struct RowDecoder {
             const uint32_t m1 = ptx::lds_u8(plane + 16u * j);
             const uint32_t m2 = ptx::lds_u8(plane + plane_stride + 16u * j);
             const uint32_t m3 = ptx::lds_u8(plane + 2u * plane_stride + 16u * j);
-            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, k128, ct));
-            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, k128, ct));
-            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, k128, ct));
+            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, kent, ct));
+            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, kent, ct));
+            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, kent, ct));
             code[j] = ptx::mad_lo(t3, k4, ptx::mad_lo(t2, k2, t1));
             flag[j] = t1 | t2 | t3;  // nibble p = 1 when position p is common
             ind[j] = m1 | m2 | m3;

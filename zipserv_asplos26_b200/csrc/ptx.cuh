@@ -136,6 +136,29 @@ __device__ __forceinline__ bool wait_global_geq(const uint32_t* p, uint32_t valu
     if (flag) atomicOr(&g_device_flags, 1u);
     return false;
 }
+// System-scope release store and bounded acquire wait for equality (flags
+// exchanged with other GPUs over NVLink). The wait gives up after limit_ns,
+// raises g_device_flags bit 0 and returns false.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool wait_global_eq_sys(const uint32_t* p, uint32_t value,
+                                                   uint64_t limit_ns) {
+    uint64_t start = 0;
+    for (uint32_t i = 0; i < (1u << 30); ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v == value) return true;
+        if ((i & 15) == 15) {
+            const uint64_t now = global_timer_ns();
+            if (!start) start = now;
+            else if (now - start > limit_ns) break;
+            __nanosleep(64);
+        }
+    }
+    atomicOr(&g_device_flags, 1u);
+    return false;
+}
 // Acquire-release increment of a global counter; returns the prior value.
 __device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t* p, uint32_t v) {
     uint32_t prior;
@@ -171,24 +194,6 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
     return p;
-}
-// Prefetch into L2 (no shared memory, no barrier): a 1-D range (16-byte
-// aligned, size a multiple of 16) and a box of a tiled tensor map.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int x, int y, int z,
-                                                int w) {
-    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z), "r"(w)
-                 : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z)
-                 : "memory");
 }
 // 2-D tiled tensor load (no multicast), completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
@@ -409,6 +414,9 @@ __device__ __forceinline__ void sts16(uint32_t a, uint32_t v) {
 }
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.b32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ void sts64(uint32_t a, int2 v) {
+    asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(a), "r"(v.x), "r"(v.y) : "memory");
 }
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y),

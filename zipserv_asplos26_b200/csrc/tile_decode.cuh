@@ -34,7 +34,7 @@
 namespace zs {
 
 struct TileDecoder {
-    uint32_t ct;        // shared address of the code table + lane * 4
+    uint32_t ct;        // shared address of the code table + (lane % kTableCopies) * 4
     uint32_t word;      // byte offset of this small tile's word in a tile's bitmap plane
     uint32_t band8;     // byte offset of band q's (common, rare) pair in a tile's band offsets
     uint32_t jx;        // j << 4: this thread's 16-byte chunk before swizzling
@@ -42,14 +42,14 @@ struct TileDecoder {
     uint32_t ord64;     // 64 * (2j + rt): elements before this small tile in its band
     uint32_t j, rt;
     uint32_t xp_lo, xp_hi;  // exponent palette (see RowDecoder)
-    uint32_t k2, k4, k8, k128, krank, khi;
+    uint32_t k2, k4, k8, kent, krank, khi;
 
     __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int q,
                                          uint32_t start_exp) {
         const uint32_t tau = uint32_t(lane) >> 4;
         rt = (uint32_t(lane) >> 3) & 1u;
         j = uint32_t(lane) & 7u;
-        ct = tables_smem + uint32_t(lane) * 4u;
+        ct = tables_smem + uint32_t(lane % kTableCopies) * 4u;
         word = (uint32_t(q) * 16u + 2u * j + rt) * 8u;
         band8 = uint32_t(q) * 8u;
         jx = j << 4;
@@ -65,7 +65,7 @@ struct TileDecoder {
         k2 = ptx::launder(2u);
         k4 = ptx::launder(4u);
         k8 = ptx::launder(8u);
-        k128 = ptx::launder(128u);
+        kent = ptx::launder(uint32_t(kTableCopies) * 4u);
         krank = ptx::launder(0x11111110u);
         khi = ptx::launder(0x10000u);
     }
@@ -108,9 +108,9 @@ struct TileDecoder {
             const uint32_t m1 = __byte_perm(r < 4 ? p1.x : p1.y, 0, sel);
             const uint32_t m2 = __byte_perm(r < 4 ? p2.x : p2.y, 0, sel);
             const uint32_t m3 = __byte_perm(r < 4 ? p3.x : p3.y, 0, sel);
-            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, k128, ct));
-            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, k128, ct));
-            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, k128, ct));
+            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, kent, ct));
+            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, kent, ct));
+            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, kent, ct));
             const uint32_t code = ptx::mad_lo(t3, k4, ptx::mad_lo(t2, k2, t1));
             const uint32_t flag = t1 | t2 | t3;
             const uint32_t aw = co & ~3u;

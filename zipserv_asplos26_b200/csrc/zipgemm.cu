@@ -67,10 +67,6 @@ constexpr int gemm_threads(int ndg) { return 256 + 128 * ndg; }
 // segments and arrive long before; the limit only matters when those CTAs
 // could not start (other work holding SMs).
 constexpr uint64_t kReducerWaitNs = 50000;
-// How far ahead (in K-slice steps of a CTA) the producers prefetch weight
-// data into L2 (even, at most 62: the offsets come from the current or the
-// next 32-step chunk of a producer).
-constexpr int kPrefetchSteps = 16;
 
 
 // TMEM lane (= decoder thread slot) -> row inside the 128-row block.
@@ -98,11 +94,97 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
 // too and whichever part arrives last sums all pieces. Either way the sum
 // runs in K order - a fixed order, so results do not depend on timing - and
 // the reducer returns the counter to zero.
+// The items are dealt out in groups of S consecutive K slices of one unit
+// (S = 2 when K/64 is even, else 1), so a CTA's range always holds whole
+// groups and each compressed slot carries one group: CTA c owns groups
+// [c * G / grid, (c + 1) * G / grid), G = steps / S.
+__device__ __forceinline__ int sched_start(int c, int grid, int groups, int S) {
+    return S * int(int64_t(c) * groups / grid);
+}
+__device__ __forceinline__ int sched_owner(int item, int grid, int groups, int S) {
+    return int((int64_t(item / S + 1) * grid - 1) / groups);
+}
 __device__ __forceinline__ int step_start(int c, const GemmParams& p) {
-    return int(int64_t(c) * p.steps / p.grid);
+    return sched_start(c, p.grid, p.groups, p.S);
 }
 __device__ __forceinline__ int step_owner(int item, const GemmParams& p) {
-    return int((int64_t(item + 1) * p.grid - 1) / p.steps);
+    return sched_owner(item, p.grid, p.groups, p.S);
+}
+
+// ----------------------------------------------------------------------
+// Fused all-reduce of the output (row-parallel layers over tp_world GPUs).
+// When a CTA holds the final FP32 value of a (unit, TMEM lane quarter) - a
+// whole unit, or a split unit it reduced - it sends the quarter's chunks to
+// every rank's receive buffer (peer stores over NVLink), raises its flag on
+// every rank, waits (bounded) for every rank's flag, sums the ranks' values
+// in rank order and stores BF16. Every rank runs the same schedule on its
+// K shard, so every rank computes every unit; the sum order is fixed, so all
+// ranks store identical outputs. Buffers are double-buffered by the launch's
+// epoch parity: a rank can be at most one launch ahead of another (it cannot
+// finish a launch without every rank's values), so the buffer it writes is
+// never the one a slower rank still reads.
+//   receive buffer: [2][world][units][4 quarters][chunks][32 lanes][16] FP32
+//   flags:          [2][world][units][4] u32 = epoch of the writing launch
+__device__ __forceinline__ size_t tp_recv_index(const GemmParams& p, uint32_t par, int src,
+                                                int unit, int q, int c, int lane) {
+    return ((((size_t(par) * p.tp_world + src) * p.units + unit) * 4 + q) * size_t(p.bn / 16) +
+            c) * 512u + size_t(lane) * 16u;
+}
+__device__ __forceinline__ size_t tp_flag_index(const GemmParams& p, uint32_t par, int src,
+                                                int unit, int q) {
+    return ((size_t(par) * p.tp_world + src) * p.units + unit) * 4 + q;
+}
+// This launch's epoch (read after the previous launch completed: every rank
+// counts its fused launches alike).
+__device__ __forceinline__ uint32_t tp_epoch(const GemmParams& p) {
+    return *reinterpret_cast<volatile uint32_t*>(p.tp_state) + 1u;
+}
+__device__ __forceinline__ void tp_put(const GemmParams& p, uint32_t epoch, int unit, int q, int c,
+                                       int lane, const float (&acc)[16]) {
+    for (int r = 0; r < p.tp_world; ++r) {
+        float* dst = p.tp_recv[r] + tp_recv_index(p, epoch & 1u, p.tp_rank, unit, q, c, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            ptx::stg_cg_f4(dst + 4 * i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2],
+                                                    acc[4 * i + 3]));
+    }
+}
+// Every chunk of (unit, q) has been put by this CTA (its warps met at a
+// barrier, or one warp put them all): publish, wait, sum, store.
+__device__ __noinline__ void tp_finish(const GemmParams& p, uint32_t epoch, int unit, int q,
+                                       int lane, int nb, int mrow, bool row_ok) {
+    __threadfence_system();
+    __syncwarp();
+    const uint32_t par = epoch & 1u;
+    if (lane < p.tp_world)
+        ptx::st_release_sys(p.tp_flags[lane] + tp_flag_index(p, par, p.tp_rank, unit, q), epoch);
+    bool ok = true;
+    if (lane < p.tp_world)
+        ok = ptx::wait_global_eq_sys(p.tp_flags[p.tp_rank] + tp_flag_index(p, par, lane, unit, q),
+                                     epoch, 2000000000ull);
+    ok = __all_sync(kFullMask, ok);
+    const float* mine = p.tp_recv[p.tp_rank];
+    for (int c = 0; c < p.bn / 16; ++c) {
+        float acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+        for (int src = 0; src < p.tp_world; ++src) {
+            const float* from = mine + tp_recv_index(p, par, src, unit, q, c, lane);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 v = ptx::ldg_cg_f4(from + 4 * i);
+                acc[4 * i] += v.x, acc[4 * i + 1] += v.y, acc[4 * i + 2] += v.z,
+                    acc[4 * i + 3] += v.w;
+            }
+        }
+        if (!row_ok || !ok) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int nn = nb * p.bn + 16 * c + j;
+            if (nn < p.n)
+                p.y[size_t(nn) * p.m + mrow] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[j]));
+        }
+    }
 }
 
 // One 16-column chunk of a resident reducer's row block: its own K part
@@ -119,6 +201,9 @@ struct ChunkReduce {
     int c0, parts, nb, mrow, lane;
     size_t piece0;  // the quarter's first piece
     bool row_ok, dok, wok;
+    const GemmParams* gp;  // fused all-reduce: chunks go to the ranks instead of y
+    uint32_t epoch;
+    int unit, q;
 
     __device__ __forceinline__ void run(int c) const {
         uint32_t v[16];
@@ -155,6 +240,10 @@ struct ChunkReduce {
                 }
             }
         }
+        if (gp->tp_world > 1) {
+            tp_put(*gp, epoch, unit, q, c, lane, acc);
+            return;
+        }
         if (!row_ok) return;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -168,22 +257,26 @@ struct ChunkReduce {
 // A decoder warp's share of its CTA's last-segment reduction (kept out of
 // line so the decoder loop's register allocation is not affected). Runs
 // only when the quarter's epilogue warp saw every other part arrive in time.
-__device__ __noinline__ void help_reduce(float* ws_partials, uint16_t* y, int m, int n, int bn,
-                                         int pieces, uint32_t tmem_cols, int grid, int steps,
-                                         uint32_t tmem, uint32_t bar_d, int unit, int s, int rbs,
-                                         int kt, int cta, int g, int q, int lane, int stride) {
+__device__ __noinline__ void help_reduce(const GemmParams* gp, float* ws_partials, uint16_t* y,
+                                         int m, int n, int bn, int pieces, uint32_t tmem_cols,
+                                         int grid, int groups, int S, uint32_t tmem, uint32_t bar_d,
+                                         int unit, int s, int rbs, int kt, int cta, int g, int q,
+                                         int lane, int stride) {
     const int b = s & 1, chunks = bn / 16, ubeg = unit * kt;
     const bool dok = ptx::mbar_wait(bar_d + 8u * uint32_t(b), uint32_t(s >> 1) & 1u);
     ptx::tc_fence_after();
     ptx::wait_prerequisites();  // output writes, as in the epilogue
-    const int last_owner = int((int64_t(ubeg + kt - 1 + 1) * grid - 1) / steps);
+    const int last_owner = sched_owner(ubeg + kt - 1, grid, groups, S);
     const int parts = last_owner - cta + 1;
     const int mrow = (unit % rbs) * 128 + lane_row(32 * q + lane);
+    const uint32_t epoch = gp->tp_world > 1 ? tp_epoch(*gp) : 0u;
     const ChunkReduce cr{ws_partials, y, m, n, bn, pieces,
                          tmem + (uint32_t(32 * q) << 16) + uint32_t(b) * tmem_cols,
                          cta, parts, unit / rbs, mrow, lane, size_t(q) * size_t(chunks),
-                         mrow < m, dok, true};
+                         mrow < m, dok, true, gp, epoch, unit, q};
     for (int c = g + 1; c < chunks; c += stride) cr.run(c);
+    // Chunks sent to other GPUs are ordered before the epilogue warp's flags.
+    if (gp->tp_world > 1) __threadfence_system();
     ptx::tc_fence_before();
 }
 
@@ -196,12 +289,12 @@ __device__ __noinline__ void help_reduce(float* ws_partials, uint16_t* y, int m,
 template <int NDG>
 __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ PlaneMaps pm,
-                   const __grid_constant__ CUtensorMap mmap, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap mmap, const __grid_constant__ GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = ptx::smem_addr(smem);
-    const uint32_t bar_full = sbase;                         // [2 * NDG] slot landed
-    const uint32_t bar_free = sbase + 8 * kMaxStages;         // [2 * NDG] slot read by its group
+    const uint32_t bar_full = sbase;                         // [nslots] slot landed
+    const uint32_t bar_free = sbase + 8 * kMaxStages;         // [nslots] slot read by its groups
     const uint32_t bar_afull = bar_free + 8 * kMaxStages;     // [na] A tile written
     const uint32_t bar_aempty = bar_afull + 8 * kMaxATiles;  // [na] A tile read by MMAs
     const uint32_t bar_xfull = bar_aempty + 8 * kMaxATiles;   // [kMaxX]
@@ -232,35 +325,39 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     // initialises the barriers (one lane per barrier) and starts the table
     // copy, and the producers fetch their first chunk of payload offsets.
     //
-    // Payload offsets: lane l of producer pi holds, for chunk c, the four
-    // `global` entries (start and end of both tile rows) of its step
-    // pi + 2 * (32c + l); the next chunk is fetched a whole chunk ahead, so
-    // the producers never wait on these global loads.
+    // Payload offsets: lane l of producer pi holds, for chunk c, the `global`
+    // entries of its slot pi + 2 * (32c + l): K tiles k .. k + S of both tile
+    // rows (the start of each of the slot's tiles and the end of the last);
+    // the next chunk is fetched a whole chunk ahead, so the producers never
+    // wait on these global loads.
     const int2* goffs = reinterpret_cast<const int2*>(p.global);
-    auto fetch_offsets = [&](int pi, int c, int2 (&v)[4]) {
+    const int nslot_items = nsteps / p.S;  // slots this CTA fills (its groups)
+    auto fetch_offsets = [&](int pi, int c, int2 (&v)[6]) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = make_int2(0, 0);
-        const int s = pi + 2 * (32 * c + lane);
-        if (s < nsteps) {
-            const int item = t_begin + s, unit = item / kt, k = item - unit * kt;
+        for (int i = 0; i < 6; ++i) v[i] = make_int2(0, 0);
+        const int sl = pi + 2 * (32 * c + lane);
+        if (sl < nslot_items) {
+            const int item = t_begin + sl * p.S, unit = item / kt, k = item - unit * kt;
             const int tr = 2 * (unit % rbs);
-            v[0] = goffs[size_t(tr) * kt + k];
-            v[1] = goffs[size_t(tr) * kt + k + 1];
-            if (tr + 1 < p.row_tiles) {
-                v[2] = goffs[size_t(tr + 1) * kt + k];
-                v[3] = goffs[size_t(tr + 1) * kt + k + 1];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                if (tr + r >= p.row_tiles) break;
+                const size_t at = size_t(tr + r) * kt + k;
+                v[3 * r] = goffs[at];
+                v[3 * r + 1] = goffs[at + 1];
+                v[3 * r + 2] = p.S == 2 ? goffs[at + 2] : v[3 * r + 1];
             }
         }
     };
-    int2 first_offs[4];
+    int2 first_offs[6];
     if (warp == 2 || warp == 3) fetch_offsets(warp - 2, 0, first_offs);
     if (warp == 0) {
         ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 2 * p.tmem_cols);
         ptx::tmem_relinquish();
     } else if (warp == 1) {
-        if (lane < 2 * NDG) {
+        if (lane < p.nslots) {
             ptx::mbar_init(bar_addr(bar_full, lane), 1);
-            ptx::mbar_init(bar_addr(bar_free, lane), 4);
+            ptx::mbar_init(bar_addr(bar_free, lane), 4u * uint32_t(p.S));  // its S steps' warps
         }
         if (lane < kMaxX) {
             ptx::mbar_init(bar_addr(bar_xfull, lane), 1);
@@ -376,135 +473,118 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         __syncwarp();
     } else if (warp < 4) {
         // ------------------------------------------------------ producers
-        // Producer pi fills the compressed slots of steps pi, pi + 2, ...
-        // (step t goes to group t % NDG, slot 2 * group + ((t / NDG) & 1))
-        // once the group has released the slot's previous contents. Per
-        // slot: one 4-D tensor load for the three bitmap planes of both tile
-        // rows, one 3-D load for the band offsets and one bulk copy per
-        // payload run, all completing on the slot's barrier. The packed
-        // weight is never written by other kernels: no prerequisite wait.
+        // A slot holds one group of S consecutive K slices (both tile rows of
+        // the block): producer pi fills the CTA's slots pi, pi + 2, ... (slot
+        // v goes to ring entry v % nslots) once the decoder groups of its
+        // previous contents released it. Per slot: one 4-D tensor load for
+        // the three bitmap planes of the S x 2 tiles, one 3-D load for their
+        // band offsets, one bulk copy per payload stream and tile row (the S
+        // tiles of a tile row are consecutive in the packed streams), and the
+        // tile-relative payload starts written into the slot header. An SM
+        // takes ~100 cycles per copy whatever its size, so S = 2 halves the
+        // copies per K slice. The packed weight is never written by other
+        // kernels: no prerequisite wait.
         const int pi = warp - 2;
         const uint64_t pol_w = ptx::policy_evict_first();
-        // Position (K slice, row block) of a step, advanced without divisions.
-        struct Pos {
-            int k, rb;
-        };
-        auto advance = [&](Pos& q, int steps) {
-            q.k += steps;
-            while (q.k >= kt) {
-                q.k -= kt;
-                if (++q.rb == rbs) q.rb = 0;
-            }
-        };
-        Pos cur{t_begin - unit0 * kt, unit0 % rbs};
-        advance(cur, pi);
-        // The step kPrefetchSteps ahead of the one being filled is prefetched
-        // into L2, so a slot's copies read L2 rather than DRAM: with two
-        // slots per decoder group, a fill must land within about one step
-        // of decoding, shorter than a DRAM round trip under load.
-        Pos pf = cur;
-        advance(pf, kPrefetchSteps);
-        int2 chunk[4], ahead[4];
+        const int S = p.S, nslots = p.nslots;
+        int kc = t_begin - unit0 * kt + pi * S, rb = unit0 % rbs;  // position of slot pi
+        while (kc >= kt) {
+            kc -= kt;
+            if (++rb == rbs) rb = 0;
+        }
+        int2 chunk[6], ahead[6];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) chunk[i] = first_offs[i];
+        for (int i = 0; i < 6; ++i) chunk[i] = first_offs[i];
         bool ok = true;
-        int last = -1;  // last step issued
-        for (int t = pi, i = 0, u = pi / NDG, g = pi % NDG; t < nsteps; t += 2, ++i) {
+        int last = -1;  // last slot issued
+        for (int v = pi, i = 0; v < nslot_items; v += 2, ++i) {
             const int ci = i & 31;
             if (ci == 0) {
                 if (i > 0) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) chunk[j] = ahead[j];
+                    for (int j = 0; j < 6; ++j) chunk[j] = ahead[j];
                 }
                 fetch_offsets(pi, (i >> 5) + 1, ahead);
             }
-            const int sidx = g * 2 + (u & 1);
-            int2 e[4], f[4];
-            // Entries of the step kPrefetchSteps ahead: lane ci + kPrefetchSteps / 2
-            // of this chunk or of the next one.
-            const int fi = ci + kPrefetchSteps / 2;
+            const int sidx = v % nslots, use = v / nslots;
+            int2 e[6];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                e[j].x = __shfl_sync(kFullMask, chunk[j].x, ci);
+            for (int j = 0; j < 6; ++j)
+                e[j].x = __shfl_sync(kFullMask, chunk[j].x, ci),
                 e[j].y = __shfl_sync(kFullMask, chunk[j].y, ci);
-                const int ax = __shfl_sync(kFullMask, chunk[j].x, fi & 31);
-                const int ay = __shfl_sync(kFullMask, chunk[j].y, fi & 31);
-                const int bx = __shfl_sync(kFullMask, ahead[j].x, fi & 31);
-                const int by = __shfl_sync(kFullMask, ahead[j].y, fi & 31);
-                f[j] = fi < 32 ? make_int2(ax, ay) : make_int2(bx, by);
+            const uint32_t slot = sbase + p.off_slots + uint32_t(sidx) * L.bytes;
+            // Everything the fill needs is computed before waiting for the
+            // slot, so only the stores and copies follow the wait (the
+            // decoders compete for issue slots; a late fill stalls them).
+            const int tr0 = 2 * rb;
+            const bool has1 = tr0 + 1 < p.row_tiles;
+            // Slot header: payload starts of tile j of tile row r inside the
+            // row's runs, clamped to the capacities (decoders stay in bounds
+            // whatever the offsets say).
+            int2 h = make_int2(0, 0);
+            if (lane < 2 * S) {
+                const int r = lane / S, j = lane - r * S;
+                const int2 st = r ? e[3] : e[0];
+                const int2 tj = j ? (r ? e[4] : e[1]) : st;
+                h = make_int2(min(max(tj.x - st.x, 0), int(uint32_t(j) * cap_c)),
+                              min(max(tj.y - st.y, 0), int(uint32_t(j) * cap_r)));
             }
+            uint32_t clen[2], rlen[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int2 st = e[3 * r], en = e[3 * r + 2];
+                const bool live = r == 0 || has1;
+                // Payload copies need 16-byte aligned sources, which the
+                // offsets of valid packed data always give.
+                clen[r] = live && (st.x & 15) == 0
+                              ? min(uint32_t(max(en.x - st.x, 0)), uint32_t(S) * cap_c) & ~15u
+                              : 0u;
+                rlen[r] = live && (st.y & 7) == 0
+                              ? (min(uint32_t(max(en.y - st.y, 0)), uint32_t(S) * cap_r) * 2u) & ~15u
+                              : 0u;
+            }
+            const uint32_t full = bar_addr(bar_full, sidx);
+            const uint32_t expect =
+                p.plane_box_bytes + 64u * uint32_t(S) + clen[0] + clen[1] + rlen[0] + rlen[1];
+            if (use >= 1 && lane == 0) ok = ptx::mbar_wait(bar_addr(bar_free, sidx), (use - 1) & 1);
+            ok = __shfl_sync(kFullMask, ok, 0) != 0;
+            if (!ok) break;
+            if (lane < 2 * S) ptx::sts64(slot + L.hdr + uint32_t(lane) * 8u, h);
+            // The header stores of lanes 0 .. 2S-1 are ordered before lane 0's
+            // arrival (release), which the decoders acquire.
+            __syncwarp();
             if (lane == 0) {
-                if (u >= 2) ok = ptx::mbar_wait(bar_addr(bar_free, sidx), ((u >> 1) - 1) & 1);
-                if (ok) {
-                    const int kc = cur.k, tr0 = 2 * cur.rb;
-                    const bool has1 = tr0 + 1 < p.row_tiles;
-                    uint32_t clen[2], rlen[2];
+                ptx::mbar_arrive_expect_tx(full, expect);
+                // Largest copies first: the slot is ready when its last byte lands.
+                if (clen[0]) ptx::bulk_g2s(slot + L.common0, p.sm + e[0].x, clen[0], full, pol_w);
+                if (clen[1]) ptx::bulk_g2s(slot + L.common1, p.sm + e[3].x, clen[1], full, pol_w);
+                if (pm.count == 1) {
+                    ptx::tma_load_4d(slot, &pm.map[0], 0, kc, tr0, 0, full, pol_w);
+                } else {
 #pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        const int2 st = e[2 * r], en = e[2 * r + 1];
-                        const bool live = r == 0 || has1;
-                        // Payload copies need 16-byte aligned sources, which
-                        // the offsets of valid packed data always give.
-                        clen[r] = live && (st.x & 15) == 0
-                                      ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
-                                      : 0u;
-                        rlen[r] = live && (st.y & 7) == 0
-                                      ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
-                                      : 0u;
-                    }
-                    const uint32_t slot = sbase + p.off_slots + uint32_t(sidx) * L.bytes;
-                    const uint32_t full = bar_addr(bar_full, sidx);
-                    ptx::mbar_arrive_expect_tx(full, p.plane_box_bytes + 64u + clen[0] + clen[1] +
-                                                         rlen[0] + rlen[1]);
-                    if (pm.count == 1) {
-                        ptx::tma_load_4d(slot, &pm.map[0], 0, kc, tr0, 0, full, pol_w);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 3; ++i)
-                            ptx::tma_load_3d(slot + uint32_t(i) * L.plane_stride, &pm.map[i], 0,
-                                             kc, tr0, full, pol_w);
-                    }
-                    ptx::tma_load_3d(slot + L.med, &mmap, 0, kc, tr0, full, pol_w);
-                    if (clen[0]) ptx::bulk_g2s(slot + L.common0, p.sm + e[0].x, clen[0], full, pol_w);
-                    if (clen[1]) ptx::bulk_g2s(slot + L.common1, p.sm + e[2].x, clen[1], full, pol_w);
-                    if (rlen[0]) ptx::bulk_g2s(slot + L.rare0, p.rare + e[0].y, rlen[0], full, pol_w);
-                    if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[2].y, rlen[1], full, pol_w);
-                    last = t;
+                    for (int pl = 0; pl < 3; ++pl)
+                        ptx::tma_load_3d(slot + uint32_t(pl) * L.plane_stride, &pm.map[pl], 0, kc,
+                                         tr0, full, pol_w);
                 }
-                if (ok && t + kPrefetchSteps < nsteps) {
-                    const bool has1 = 2 * pf.rb + 1 < p.row_tiles;
-                    if (pm.count == 1) ptx::tma_prefetch_4d(&pm.map[0], 0, pf.k, 2 * pf.rb, 0);
-                    else
-                        for (int i = 0; i < 3; ++i)
-                            ptx::tma_prefetch_3d(&pm.map[i], 0, pf.k, 2 * pf.rb);
-                    ptx::tma_prefetch_3d(&mmap, 0, pf.k, 2 * pf.rb);
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        const int2 st = f[2 * r], en = f[2 * r + 1];
-                        if (r == 1 && !has1) break;
-                        const uint32_t cl = (st.x & 15) == 0
-                                                ? min(uint32_t(max(en.x - st.x, 0)), cap_c) & ~15u
-                                                : 0u;
-                        const uint32_t rl = (st.y & 7) == 0
-                                                ? (min(uint32_t(max(en.y - st.y, 0)), cap_r) * 2u) & ~15u
-                                                : 0u;
-                        if (cl) ptx::bulk_prefetch_l2(p.sm + st.x, cl);
-                        if (rl) ptx::bulk_prefetch_l2(p.rare + st.y, rl);
-                    }
-                }
+                if (rlen[0]) ptx::bulk_g2s(slot + L.rare0, p.rare + e[0].y, rlen[0], full, pol_w);
+                if (rlen[1]) ptx::bulk_g2s(slot + L.rare1, p.rare + e[3].y, rlen[1], full, pol_w);
+                ptx::tma_load_3d(slot + L.med, &mmap, 0, kc, tr0, full, pol_w);
             }
-            if (!__shfl_sync(kFullMask, ok, 0)) break;
-            advance(cur, 2);
-            advance(pf, 2);
-            if ((g += 2) >= NDG) g -= NDG, ++u;
+            last = v;
+            for (kc += 2 * S; kc >= kt;) {
+                kc -= kt;
+                if (++rb == rbs) rb = 0;
+            }
         }
-        // Never leave copies in flight: wait (bounded) for the last use of
-        // every slot this producer filled.
-        if (lane == 0)
-            for (int t = max(pi, last - 2 * NDG + 2); t >= 0 && t <= last; t += 2) {
-                const int g = t % NDG, u = t / NDG;
-                ptx::mbar_wait(bar_addr(bar_full, g * 2 + (u & 1)), (u >> 1) & 1);
-            }
+        // Never leave copies in flight: wait (bounded) for this producer's
+        // slots that are the last use of their ring entry (with an odd ring
+        // the producers alternate on an entry, and waiting on an earlier use
+        // after a later one landed would target a phase already passed).
+        if (lane == 0) {
+            const int end = ok ? nslot_items : last + 1;
+            for (int v = max(0, end - nslots); v < end; ++v)
+                if ((v & 1) == pi) ptx::mbar_wait(bar_addr(bar_full, v % nslots), (v / nslots) & 1);
+        }
         __syncwarp();
     } else if (warp < kEpiWarp) {
         // ------------------------------------------------------ decoders
@@ -524,18 +604,21 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             if (++rb == rbs) rb = 0;
         }
         int a = g, ause = 0;  // A tile t % na and its use t / na
-        for (int t = g, u = 0; t < nsteps; t += NDG, ++u) {
+        for (int t = g; t < nsteps; t += NDG) {
             const bool valid = tau == 0 || 2 * rb + 1 < p.row_tiles;
-            const int sidx = g * 2 + (u & 1);
+            const int v = t / p.S, j = t - v * p.S;  // slot v, its K slice j
+            const int sidx = v % p.nslots, use = v / p.nslots;
             const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
-            ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), (u >> 1) & 1);
+            ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), use & 1);
             // A tile a = t % na is free once the MMAs of step t - na finished.
             if (ause > 0) ok = ok && ptx::mbar_wait(bar_addr(bar_aempty, a), (ause - 1) & 1);
             if (!__all_sync(kFullMask, ok)) break;
-            dec.decode_store(slot + uint32_t(tau) * L.plane1, L.plane_stride,
-                             slot + L.med + uint32_t(tau) * 32u,
-                             slot + (tau ? L.common1 : L.common0), slot + (tau ? L.rare1 : L.rare0),
-                             cap_c, cap_r, abase + uint32_t(a) * kATileBytes, valid);
+            const uint32_t tile = uint32_t(tau * p.S + j);  // the tile's index in the slot
+            const int2 h = ptx::lds_s64(slot + L.hdr + tile * 8u);
+            dec.decode_store(slot + tile * L.plane1, L.plane_stride, slot + L.med + tile * 32u,
+                             slot + (tau ? L.common1 : L.common0) + uint32_t(h.x),
+                             slot + (tau ? L.rare1 : L.rare0) + 2u * uint32_t(h.y), cap_c, cap_r,
+                             abase + uint32_t(a) * kATileBytes, valid);
             // Generic-proxy stores must be visible to the tensor cores.
             ptx::fence_proxy_async_smem();
             __syncwarp();
@@ -563,8 +646,9 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
                 const bool fast = ptx::lds_s32(verdict + 4u * uint32_t(q)) != 0;
                 if (fast && g + 1 < chunks)
-                    help_reduce(p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, p.tmem_cols, p.grid,
-                                p.steps, tmem, bar_d, unit, s, rbs, kt, cta, g, q, lane, 1 + NDG);
+                    help_reduce(&p, p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, p.tmem_cols,
+                                p.grid, p.groups, p.S, tmem, bar_d, unit, s, rbs, kt, cta, g, q,
+                                lane, 1 + NDG);
                 ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
             }
         }
@@ -580,6 +664,8 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         // Output and workspace writes must not race the kernels this one
         // depends on (they may still read those buffers).
         ptx::wait_prerequisites();
+        const bool tp = p.tp_world > 1;
+        const uint32_t epoch = tp ? tp_epoch(p) : 0u;
         auto store_row = [&](int nb, int c, int mrow, const float (&acc)[16]) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -606,11 +692,13 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                     float acc[16];
 #pragma unroll
                     for (int j = 0; j < 16; ++j) acc[j] = dok ? __uint_as_float(v[j]) : 0.f;
-                    if (row_ok) store_row(nb, c, mrow, acc);
+                    if (tp) tp_put(p, epoch, unit, q, c, lane, acc);
+                    else if (row_ok) store_row(nb, c, mrow, acc);
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));
+                if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
                 continue;
             }
             // Partial segments are a CTA's first or last: slot `which`.
@@ -643,12 +731,15 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                     // Chunks 0, 1 + NDG, ...; the quarter's decoder warps take
                     // the others (this is the CTA's last segment, they are idle).
                     const ChunkReduce cr{p.ws_partials, p.y, p.m, p.n, p.bn, p.pieces, tbase, c0,
-                                         parts, nb, mrow, lane, piece0, row_ok, dok, true};
+                                         parts, nb, mrow, lane, piece0, row_ok, dok, true,
+                                         &p, epoch, unit, q};
                     // With one chunk (N tile 16) the epilogue warp works alone.
                     const int stride = chunks > 1 ? 1 + NDG : 1;
                     for (int c = 0; c < chunks; c += stride) cr.run(c);
                     ptx::tc_fence_before();
                     if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
+                    // The helpers' chunks were sent before the barrier.
+                    if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
                     else __syncwarp();
                     if (lane == 0) {
                         ptx::mbar_arrive(bar_addr(bar_tempty, b));
@@ -707,10 +798,12 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                         acc[4 * i + 2] += v.z, acc[4 * i + 3] += v.w;
                     }
                 }
-                if (row_ok) store_row(nb, c, mrow, acc);
+                if (tp) tp_put(p, epoch, unit, q, c, lane, acc);
+                else if (row_ok) store_row(nb, c, mrow, acc);
             }
             __syncwarp();
             if (lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
+            if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
         }
     }
 
@@ -718,6 +811,15 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     if (warp == 0) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, 2 * p.tmem_cols);
+    }
+    // Fused all-reduce: the last CTA to finish advances this rank's epoch
+    // (every CTA read it in its epilogue, before this point).
+    if (p.tp_world > 1 && tid == 0) {
+        __threadfence();
+        if (atomicAdd(p.tp_state + 1, 1u) == uint32_t(p.grid - 1)) {
+            p.tp_state[1] = 0u;
+            p.tp_state[0] = tp_epoch(p);
+        }
     }
 }
 
@@ -774,27 +876,39 @@ uint32_t round_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 struct GemmLayout {
     uint32_t off_a, off_x, off_slots, x_bytes, total;
     SlotLayout slot;
-    int nx;
+    int nx, nslots;
 };
 
 // Shared memory: barriers | lookup tables | A tiles (na 16 KB 128 x 64
 // BF16 tiles, 1024-aligned) | x ring (nx slots of bn*128
-// bytes) | compressed slots (two per group) | pad. The x ring gets one slot
-// per A tile when they fit (then an x slot is freed by the same commit as
-// its A tile), else as many as fit.
+// bytes) | compressed slots (2 * ndg / S, each S K slices: two K slices'
+// worth per decoder group) | pad. The x ring gets one slot per A tile when
+// they fit (then an x slot is freed by the same commit as its A tile), else
+// as many as fit.
 GemmLayout gemm_layout(int ndg, int na, int bn, uint32_t plane_pitch, uint32_t cap_c,
-                       uint32_t cap_r, int smem_limit) {
+                       uint32_t cap_r, int smem_limit, int S) {
     GemmLayout l{};
     l.off_a = round_up(kBarrierBytes + kTableBytes, 1024);
     l.off_x = l.off_a + uint32_t(na) * kATileBytes;
     l.x_bytes = uint32_t(bn) * 128;
-    l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r);
-    const uint32_t slots = uint32_t(2 * ndg) * l.slot.bytes;
-    const uint32_t used = l.off_x + slots + kRingPadBytes;
-    const uint32_t avail = uint32_t(smem_limit) > used ? uint32_t(smem_limit) - used : 0;
-    l.nx = std::min<int>({kMaxX, na, int(avail / l.x_bytes)});
+    l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r, S);
+    // At least two K slices of compressed data per decoder group; the x ring
+    // then takes one slot per A tile if it fits (two at least), and what is
+    // left goes to more compressed slots (a deeper ring hides the refill
+    // latency: a slot is refilled only after its last reader released it).
+    const int min_slots = 2 * ndg / S;
+    const uint32_t base = l.off_x + kRingPadBytes;
+    const auto fits = [&](int nx, int ns) {
+        return base + uint32_t(nx) * l.x_bytes + uint32_t(ns) * l.slot.bytes <=
+               uint32_t(smem_limit);
+    };
+    l.nx = 0;
+    for (int nx = std::min(kMaxX, na); nx >= 2 && !l.nx; --nx)
+        if (fits(nx, min_slots)) l.nx = nx;
+    l.nslots = min_slots;
+    while (l.nx && l.nslots < kMaxStages && fits(l.nx, l.nslots + 1)) ++l.nslots;
     l.off_slots = l.off_x + uint32_t(l.nx) * l.x_bytes;
-    l.total = l.off_slots + slots + kRingPadBytes;
+    l.total = l.off_slots + uint32_t(l.nslots) * l.slot.bytes + kRingPadBytes;
     return l;
 }
 
@@ -802,24 +916,28 @@ GemmLayout gemm_layout(int ndg, int na, int bn, uint32_t plane_pitch, uint32_t c
 
 int device_sm_count(int device) { return device_info(device).sms; }
 
-SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r) {
-    // One K slice of two tile rows. A bitmap plane's tile occupies
-    // plane_pitch bytes: the tensor load's box is wider than the 64-word
-    // tile (the words past it zero-filled), which puts tile row 1 off tile
-    // row 0 modulo 128 bytes, so the half-warps decoding the two tile rows
-    // read different banks (528: 16 bytes off, enough for the decoder's
-    // byte loads, which touch four banks per half-warp; 576: 64 bytes off,
-    // with every plane 128-byte aligned as separate tensor loads require).
+SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r, int S) {
+    // S K slices of two tile rows: 2S tiles, tile (row r, slice j) at index
+    // r*S + j. A bitmap plane's tile occupies plane_pitch bytes: the tensor
+    // load's box is wider than the 64-word tile (the words past it
+    // zero-filled), which puts consecutive tiles off each other modulo 128
+    // bytes, so lanes decoding different tiles read different banks (528:
+    // 16 bytes off; 576: 64 bytes off, with every plane 128-byte aligned as
+    // separate tensor loads require). Then the tiles' band offsets (32 B
+    // each), a header of tile-relative payload starts ([2][S] int2, written
+    // by the producer), and per tile row one common and one rare run of its S
+    // tiles (the row-1 runs 64 bytes further modulo 128).
     SlotLayout s{};
+    const uint32_t us = uint32_t(S);
     s.plane1 = plane_pitch;
-    s.plane_stride = 2u * plane_pitch;
-    s.med = round_up(3u * s.plane_stride, 128);  // [2][32 B]
-    s.hdr = 0;                                   // unused: one slice per slot
-    s.common0 = round_up(s.med + 64u, 128);
-    s.common1 = s.common0 + cap_c + 64;  // cap_c is a multiple of 128
-    s.rare0 = round_up(s.common1 + cap_c, 16);
-    s.rare1 = s.rare0 + cap_r * 2;
-    s.bytes = round_up(s.rare1 + cap_r * 2, 128);
+    s.plane_stride = 2u * us * plane_pitch;
+    s.med = round_up(3u * s.plane_stride, 128);  // [2S][32 B]
+    s.hdr = s.med + 64u * us;                    // [2S] int2
+    s.common0 = round_up(s.hdr + 16u * us, 128);
+    s.common1 = s.common0 + us * cap_c + 64;  // cap_c is a multiple of 128
+    s.rare0 = round_up(s.common1 + us * cap_c, 16);
+    s.rare1 = s.rare0 + us * cap_r * 2;
+    s.bytes = round_up(s.rare1 + us * cap_r * 2, 128);
     return s;
 }
 
@@ -906,7 +1024,7 @@ static cudaError_t ensure_gemm_attributes(int device) {
 
 // The persistent schedule of one launch (see the kernel's work schedule).
 struct Schedule {
-    int bn, row_blocks, units, steps, grid, pieces;
+    int bn, row_blocks, units, steps, S, groups, grid, pieces;
     bool partial;  // some CTA range splits a unit: the fixup workspace is used
 };
 
@@ -917,12 +1035,18 @@ static Schedule make_schedule(int m, int n, int k, int kparts, int sms) {
     s.row_blocks = (m / 64 + 1) / 2;
     s.units = s.row_blocks * ((n + s.bn - 1) / s.bn);
     s.steps = s.units * kt;
+    // K slices per slot. Two slices per slot (half the copies per slice)
+    // measured no faster on B200 than one (the fills are limited by how fast
+    // data lands, not by copy issue), and a slot shared by two decoder
+    // groups is released later; so one.
+    s.S = 1;
+    s.groups = s.steps / s.S;
     const int64_t want = kparts > 0 ? int64_t(s.units) * kparts : int64_t(std::max(1, sms));
-    s.grid = int(std::max<int64_t>(1, std::min<int64_t>(want, s.steps)));
+    s.grid = int(std::max<int64_t>(1, std::min<int64_t>(want, s.groups)));
     s.pieces = s.bn / 4;
     s.partial = false;
     for (int c = 1; c < s.grid && !s.partial; ++c)
-        if ((int64_t(c) * s.steps / s.grid) % kt) s.partial = true;
+        if ((int64_t(s.S) * (int64_t(c) * s.groups / s.grid)) % kt) s.partial = true;
     return s;
 }
 
@@ -1030,6 +1154,14 @@ std::atomic<uint64_t> g_reducer_wait_ns{kReducerWaitNs};
 
 uint64_t set_reducer_wait_ns(uint64_t ns) { return g_reducer_wait_ns.exchange(ns); }
 
+void allreduce_exchange_bytes(int m, int n, int world, size_t* recv_bytes, size_t* flag_bytes) {
+    *recv_bytes = *flag_bytes = 0;
+    if (!valid_matrix(m, 64) || n <= 0 || world < 2 || world > kMaxTp) return;
+    const Schedule s = make_schedule(m, n, 64, 0, 1);  // units and N tile do not depend on K
+    *recv_bytes = size_t(2) * world * s.units * s.bn * 128u * sizeof(float);
+    *flag_bytes = (size_t(2) * world * s.units * 4u * sizeof(uint32_t) + 15u) / 16u * 16u;
+}
+
 int plan_kparts(int m, int n, int k, int device) {
     if (!valid_matrix(m, k) || n <= 0) return -1;
     const Schedule s = make_schedule(m, n, k, 0, device_info(device).sms);
@@ -1048,7 +1180,8 @@ void gemm_workspace_bytes(int m, int n, int k, int kparts, int device, size_t* p
 cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
                            const void* b2, const void* b3, const void* medium, const void* global,
                            int max_common, int max_rare, int start_exp, const void* x, void* y,
-                           int m, int n, int k, int kparts, const GemmScratch* scratch) {
+                           int m, int n, int k, int kparts, const GemmScratch* scratch,
+                           const TpExchange* tp) {
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);
     if (e != cudaSuccess) return e;
@@ -1065,6 +1198,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.y = static_cast<uint16_t*>(y);
     p.m = m, p.n = n, p.k = k, p.kt = kt, p.row_tiles = m / 64;
     p.row_blocks = sched.row_blocks, p.units = sched.units, p.steps = sched.steps;
+    p.S = sched.S, p.groups = sched.groups;
     p.grid = sched.grid, p.pieces = sched.pieces;
     // One CTA per SM (the shared-memory footprint allows no more): with at
     // most one CTA per SM every CTA of the grid normally runs at the same
@@ -1073,6 +1207,14 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     // last-arrival reduction.
     p.resident = sched.grid <= d.sms ? 1 : 0;
     p.reducer_wait_ns = g_reducer_wait_ns.load(std::memory_order_relaxed);
+    if (tp && tp->world > 1) {
+        p.tp_world = tp->world, p.tp_rank = tp->rank;
+        for (int r = 0; r < tp->world; ++r) {
+            p.tp_recv[r] = static_cast<float*>(tp->recv[r]);
+            p.tp_flags[r] = static_cast<uint32_t*>(tp->flags[r]);
+        }
+        p.tp_state = static_cast<uint32_t*>(tp->state);
+    }
     p.bn = sched.bn;
     if (sched.partial) {
         const size_t need_p = schedule_partial_bytes(sched), need_c = schedule_counter_bytes(sched);
@@ -1106,20 +1248,21 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     const bool spaced = a2 > a1 && a2 - a1 == a3 - a2 && (a2 - a1) % 16 == 0 &&
                         a2 - a1 < (uint64_t(1) << 40);  // the test encode_plane_maps makes
     uint32_t pitch = spaced ? 528 : 576;
-    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), pitch / 8, 1, 2)) {
+    const uint32_t S = uint32_t(sched.S);
+    if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), pitch / 8, S, 2)) {
         pitch = 512;
-        if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 64, 1, 2)) {
+        if (!encode_plane_maps(&pm, b1, b2, b3, uint64_t(kt), uint64_t(m / 64), 64, S, 2)) {
             zs_set_error("zipgemm: bitmap tensor maps rejected (bitmaps must be 16-byte aligned)");
             return cudaErrorInvalidValue;
         }
     }
-    p.plane_box_bytes = 3u * 2u * pitch;
+    p.plane_box_bytes = 3u * 2u * S * pitch;
     // Band offsets as [row tiles][k tiles][4 u64]: one box = both tile rows.
     CUtensorMap mmap;
     {
         const cuuint64_t dims[3] = {4, uint64_t(kt), uint64_t(m / 64)};
         const cuuint64_t strides[2] = {32, uint64_t(kt) * 32};
-        const cuuint32_t box[3] = {4, 1, 2};
+        const cuuint32_t box[3] = {4, S, 2};
         if (!encode_map(&mmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, medium, 3, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_NONE)) {
             zs_set_error("zipgemm: band-offset tensor map rejected (must be 16-byte aligned)");
@@ -1137,7 +1280,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     int ndg = 0;
     GemmLayout l{};
     for (const Choice& c : kChoices) {
-        l = gemm_layout(c.ndg, c.na, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin);
+        l = gemm_layout(c.ndg, c.na, p.bn, pitch, p.cap_c, p.cap_r, d.smem_optin, sched.S);
         if (l.nx >= 2) {
             ndg = c.ndg;
             p.na = c.na;
@@ -1149,6 +1292,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
         return cudaErrorInvalidConfiguration;
     }
     p.nx = l.nx;
+    p.nslots = l.nslots;
     p.off_a = l.off_a, p.off_x = l.off_x;
     p.off_slots = l.off_slots, p.x_bytes = l.x_bytes, p.slot = l.slot;
     // TMEM holds two FP32 accumulators of bn columns (consecutive segments

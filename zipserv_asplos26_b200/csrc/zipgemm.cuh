@@ -14,6 +14,7 @@ constexpr int kBarrierBytes = 1024;
 constexpr int kChunk = 32;       // K slices per refill of the offset / band-offset caches
 constexpr int kMaxGroup = 8;     // tiles per half of a compressed ring slot
 constexpr uint32_t kATileBytes = 128 * 128;  // decoded A tile: 128 rows x 64 BF16
+constexpr int kMaxTp = 8;        // ranks of a fused all-reduce
 
 // A compressed ring slot holds two runs ("halves") of up to kMaxGroup tiles
 // that are consecutive in the packed streams (the fused GEMM: two tile rows
@@ -29,7 +30,7 @@ constexpr uint32_t kATileBytes = 128 * 128;  // decoded A tile: 128 rows x 64 BF
 struct SlotLayout {
     uint32_t plane_stride, plane1, med, hdr, common0, common1, rare0, rare1, bytes;
 };
-SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r);
+SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r, int S);
 SlotLayout decompress_slot_layout(int half, uint32_t cap_c, uint32_t cap_r);
 
 struct GemmParams {
@@ -45,7 +46,10 @@ struct GemmParams {
     int row_blocks;        // 128-row blocks: ceil(row_tiles / 2)
     int units;             // row_blocks * n blocks
     int steps;             // units * kt: the (unit, K slice) work items
-    int grid;              // CTAs; CTA c owns items [c*steps/grid, (c+1)*steps/grid)
+    int S;                 // K slices per compressed slot (2 when kt is even, else 1)
+    int groups;            // steps / S: the items are dealt out S at a time
+    int nslots;            // compressed slots in the ring (2 * decoder groups / S)
+    int grid;              // CTAs; CTA c owns items [S*(c*groups/grid), S*((c+1)*groups/grid))
     int pieces;            // 32-row x 16-column pieces of a unit's tile: 4 * bn / 16
     int resident;          // 1: every CTA runs at once (grid <= SMs), so the first
                            // part's CTA may wait for a unit's other parts
@@ -58,9 +62,17 @@ struct GemmParams {
     uint32_t plane_box_bytes;  // bytes one bitmap tensor load (or three) writes
     uint32_t off_a, off_x, off_slots;
     uint32_t x_bytes;      // one x slot: bn tokens x one K slice (bn * 128 bytes)
-    SlotLayout slot;       // one K slice of the block's two tile rows
+    SlotLayout slot;       // S K slices of the block's two tile rows
     uint32_t tmem_cols;    // columns of one accumulator (two are allocated)
     uint64_t reducer_wait_ns;  // how long a row block's first part waits for the others
+    // Fused all-reduce of the output over tp_world ranks (row-parallel
+    // layers; tp_world <= 1: off). tp_recv[r] / tp_flags[r] are rank r's
+    // receive buffer and flags as this GPU addresses them (peer memory);
+    // tp_state is this rank's [epoch, finished CTAs] pair.
+    int tp_world, tp_rank;
+    float* tp_recv[kMaxTp];
+    uint32_t* tp_flags[kMaxTp];
+    uint32_t* tp_state;
 };
 
 struct DecompressParams {
@@ -100,11 +112,23 @@ struct GemmScratch {
 // Launch the fused kernel. `kparts` = 0: one CTA per SM (or fewer for small
 // problems); kparts > 0: kparts CTAs per 128-row block. `scratch` null: the
 // library's own per-stream scratch. Arguments are assumed validated.
+struct TpExchange;
 cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare, const void* b1,
                            const void* b2, const void* b3, const void* medium, const void* global,
                            int max_common, int max_rare, int start_exp, const void* x, void* y,
-                           int m, int n, int k, int kparts, const GemmScratch* scratch = nullptr);
+                           int m, int n, int k, int kparts, const GemmScratch* scratch = nullptr,
+                           const TpExchange* tp = nullptr);
 int plan_kparts(int m, int n, int k, int device);
+// Fused all-reduce exchange of one launch: the peers' receive buffers and
+// flags (index = rank) and this rank's state pair; sizes checked by the caller.
+struct TpExchange {
+    int world, rank;
+    void* const* recv;
+    void* const* flags;
+    void* state;
+};
+// Receive buffer and flag bytes a fused all-reduce of an [n, m] output needs.
+void allreduce_exchange_bytes(int m, int n, int world, size_t* recv_bytes, size_t* flag_bytes);
 // How long (ns) the CTA holding a split row block's first K part waits for
 // the other parts before falling back to the last-arrival reduction (both
 // give identical results). Returns the previous value.

@@ -123,11 +123,15 @@ class DecodeStep:
         self.cos = torch.cat((ang.cos(), ang.cos())).to(torch.bfloat16)
         self.sin = torch.cat((ang.sin(), ang.sin())).to(torch.bfloat16)
         self.scale = 1.0 / math.sqrt(hd)
+        self.exchange = None
 
     @classmethod
-    def packed_from(cls, dense: "DecodeStep", pack=None, linear=None) -> "DecodeStep":
+    def packed_from(cls, dense: "DecodeStep", pack=None, linear=None,
+                    exchange=None) -> "DecodeStep":
         """The "zipgemm" twin of a dense model: the same weights packed on the
-        GPU, sharing the embedding and the KV cache."""
+        GPU, sharing the embedding and the KV cache. With a tp.PeerExchange,
+        the row-parallel o and down projections sum their outputs across
+        ranks inside the fused kernel instead of with an all-reduce."""
         if dense.mode != "dense":
             raise ValueError("packed_from needs a dense model")
         twin = cls.__new__(cls)
@@ -137,6 +141,7 @@ class DecodeStep:
         twin._linear = linear or runtime.linear
         twin.layers = [{name: twin._pack(w) for name, w in layer.items()} for layer in dense.layers]
         twin.lm_head = twin._pack(dense.lm_head)
+        twin.exchange = exchange
         return twin
 
     def _weight(self, w: Tensor):
@@ -167,6 +172,13 @@ class DecodeStep:
             dist.all_reduce(y, group=self.group)
         return y
 
+    def _row(self, x: Tensor, w) -> Tensor:
+        """Row-parallel linear summed over ranks (inside the kernel when an
+        exchange is set, else an all-reduce after it)."""
+        if self.exchange is not None and isinstance(w, runtime.PackedWeight):
+            return self.exchange.linear(x, w)
+        return self._reduce(self._lin(x, w))
+
     def logits(self, tokens: Tensor) -> Tensor:
         """[B] token ids -> this rank's [B, vocab_rank] logits (FP32, padding -inf)."""
         s, hd = self.shape, self.shape.head_dim
@@ -183,11 +195,11 @@ class DecodeStep:
             kc[:, :, s.context] = self._rope(k)
             vc[:, :, s.context] = v
             attn = F.scaled_dot_product_attention(q, kc, vc, scale=self.scale, enable_gqa=True)
-            h = h + self._reduce(self._lin(attn.reshape(b, self.hq * hd), L["o"]))
+            h = h + self._row(attn.reshape(b, self.hq * hd), L["o"])
             x = self._norm(h)
             gu = self._lin(x, L["gate_up"])
             a = F.silu(gu[:, :self.fl]) * gu[:, self.fl:]
-            h = h + self._reduce(self._lin(a, L["down"]))
+            h = h + self._row(a, L["down"])
         logits = self._lin(self._norm(h), self.lm_head).float()
         cols = torch.arange(self.vocab_rank, device=logits.device) + self.vocab_begin
         return logits.masked_fill(cols >= s.vocab, float("-inf"))

@@ -81,6 +81,13 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "zipserv_mm_workspace_size": (_I, [_I] * 4 + [ctypes.POINTER(_U64)] * 2),
     "zipserv_device_flags": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
     "zipserv_mm_reducer_wait": (_U64, [_U64]),
+    "zipserv_mm_allreduce_sizes": (_I, [_I, _I, _I, ctypes.POINTER(_U64), ctypes.POINTER(_U64)]),
+    "zipserv_mm_allreduce": (_I, _GEMM_HEAD + [_I, _I, _P, _P, _P, _U64, _U64]),
+    "zipserv_ipc_alloc": (_I, [_U64, ctypes.POINTER(_P)]),
+    "zipserv_ipc_free": (_I, [_P]),
+    "zipserv_ipc_handle": (_I, [_P, _P]),
+    "zipserv_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "zipserv_ipc_close": (_I, [_P]),
     "zipserv_pack_device_scratch_bytes": (_U64, []),
     "zipserv_pack_device_plan": (_I, [_P, _P, _I, _I, _I, _P, _P, ctypes.POINTER(ctypes.c_int32)]),
     "zipserv_pack_device_encode": (_I, [_P, _P, _I, _I, _P, _P] + [_P] * 6),

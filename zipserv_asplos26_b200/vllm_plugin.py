@@ -5,7 +5,7 @@ vLLM-facing interface, kept as the reference plugin defines it
 (integrations/vllm/zipserv_vllm/vllm_plugin.py:43-259) so deployments switch
 by import: quantization config name "zipserv", the config keys (split_k,
 ignore, dispatch, large_batch_tokens, workspace_bytes, partial_dtype,
-decode_workspace_bytes, quant_method, checkpoint_format), the classes
+decode_workspace_bytes, per_shape_threshold, quant_method, checkpoint_format), the classes
 ``ZipServConfig`` / ``ZipServLinearMethod``, BF16-only weight loading on the
 host, the seven ``zipserv_<stream>`` buffers and the ``zipserv_*`` layer
 attributes, dense fallback with a logged reason, and the forward through the
@@ -43,6 +43,7 @@ from vllm.model_executor.utils import set_weight_attrs
 from .bf16_policy import (
     DispatchSettings,
     decode_budget_rejection,
+    fused_token_limit,
     select_split,
     startup_rejection,
 )
@@ -59,7 +60,7 @@ logger = logging.getLogger(__name__)
 DEFAULT_DISPATCH = DispatchSettings()
 # Config keys forwarded to DispatchSettings (the planner validates them).
 _DISPATCH_KNOBS = ("large_batch_tokens", "workspace_bytes", "partial_dtype",
-                   "decode_workspace_bytes")
+                   "decode_workspace_bytes", "per_shape_threshold")
 _PLANNED_GRAPH_MODES = ("NONE", "FULL_DECODE_ONLY")
 
 
@@ -177,12 +178,12 @@ def _admission(m: int, k: int, split_k: int, settings: DispatchSettings,
     if budget.compile_mode != 0 or budget.graph_mode not in _PLANNED_GRAPH_MODES:
         raise ValueError("Planned BF16 dispatch requires compilation mode 0 and eager or "
                          "full-decode-only CUDA graphs")
-    fused_max = (min(budget.max_tokens, settings.large_batch_tokens)
-                 if type(budget.max_tokens) is int else None)
+    limit = fused_token_limit(m, k, settings)
+    fused_max = min(budget.max_tokens, limit) if type(budget.max_tokens) is int else None
     reason = (startup_rejection(m, k, 1, fused_max)
               or decode_budget_rejection(m, k, settings))
     if reason is None and budget.graph_mode == "FULL_DECODE_ONLY" and not (
-            type(budget.graph_max) is int and 1 <= budget.graph_max <= settings.large_batch_tokens):
+            type(budget.graph_max) is int and 1 <= budget.graph_max <= limit):
         # The decode route cannot be captured, so every captured size must
         # stay on the fused route.
         reason = ("Decode graph capture maximum must be positive and within the fused token "
@@ -328,7 +329,7 @@ class ZipServLinearMethod(LinearMethodBase):
                                             layer.zipserv_sm_count, layer.zipserv_stock_gemm)
         logger.warning("ZipServ %s dispatch for %s: fused through %s tokens, larger batches "
                        "decode the weight (%s bytes) and use stock GEMM outside graph capture",
-                       settings.mode, (m, k), settings.large_batch_tokens, m * k * 2)
+                       settings.mode, (m, k), fused_token_limit(m, k, settings), m * k * 2)
 
     def apply(self, layer: nn.Module, x: Tensor, bias: Tensor | None = None) -> Tensor:
         route = getattr(layer, "zipserv_route", None)
