@@ -150,14 +150,21 @@ __device__ __forceinline__ void tp_put(const GemmParams& p, uint32_t epoch, int 
     }
 }
 // Every chunk of (unit, q) has been put by this CTA (its warps met at a
-// barrier, or one warp put them all): publish, wait, sum, store.
-__device__ __noinline__ void tp_finish(const GemmParams& p, uint32_t epoch, int unit, int q,
-                                       int lane, int nb, int mrow, bool row_ok) {
+// barrier, or one warp put them all): raise this rank's flag on every rank.
+__device__ __forceinline__ void tp_publish(const GemmParams& p, uint32_t epoch, int unit, int q,
+                                           int lane) {
     __threadfence_system();
     __syncwarp();
-    const uint32_t par = epoch & 1u;
     if (lane < p.tp_world)
-        ptx::st_release_sys(p.tp_flags[lane] + tp_flag_index(p, par, p.tp_rank, unit, q), epoch);
+        ptx::st_release_sys(p.tp_flags[lane] + tp_flag_index(p, epoch & 1u, p.tp_rank, unit, q),
+                            epoch);
+}
+// Wait (bounded) for every rank's pieces of (unit, q), sum them in rank
+// order and store BF16. Called once the CTA has published all its units, so
+// the wait overlaps the other ranks' remaining work rather than this one's.
+__device__ __noinline__ void tp_collect(const GemmParams& p, uint32_t epoch, int unit, int q,
+                                        int lane, int nb, int mrow, bool row_ok) {
+    const uint32_t par = epoch & 1u;
     bool ok = true;
     if (lane < p.tp_world)
         ok = ptx::wait_global_eq_sys(p.tp_flags[p.tp_rank] + tp_flag_index(p, par, lane, unit, q),
@@ -604,10 +611,12 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             if (++rb == rbs) rb = 0;
         }
         int a = g, ause = 0;  // A tile t % na and its use t / na
+        // Slot v = t / S, slice j = t % S, ring entry v % nslots and its use
+        // v / nslots, all advanced without divisions.
+        const int S = p.S, nslots = p.nslots;
+        int j = g % S, sidx = (g / S) % nslots, use = (g / S) / nslots;
         for (int t = g; t < nsteps; t += NDG) {
             const bool valid = tau == 0 || 2 * rb + 1 < p.row_tiles;
-            const int v = t / p.S, j = t - v * p.S;  // slot v, its K slice j
-            const int sidx = v % p.nslots, use = v / p.nslots;
             const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
             ok = ok && ptx::mbar_wait(bar_addr(bar_full, sidx), use & 1);
             // A tile a = t % na is free once the MMAs of step t - na finished.
@@ -627,6 +636,10 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 ptx::mbar_arrive(bar_addr(bar_afull, a));
             }
             if ((a += NDG) >= na) a -= na, ++ause;
+            for (j += NDG; j >= S;) {
+                j -= S;
+                if (++sidx == nslots) sidx = 0, ++use;
+            }
             for (k += NDG; k >= kt;) {
                 k -= kt;
                 if (++rb == rbs) rb = 0;
@@ -666,6 +679,10 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         ptx::wait_prerequisites();
         const bool tp = p.tp_world > 1;
         const uint32_t epoch = tp ? tp_epoch(p) : 0u;
+        // Fused all-reduce: segments whose final value this CTA published
+        // (collected after the loop; at most 64 segments per CTA, see the
+        // host launcher).
+        uint64_t owned = 0;
         auto store_row = [&](int nb, int c, int mrow, const float (&acc)[16]) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -698,7 +715,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));
-                if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
+                if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
                 continue;
             }
             // Partial segments are a CTA's first or last: slot `which`.
@@ -739,7 +756,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                     ptx::tc_fence_before();
                     if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
                     // The helpers' chunks were sent before the barrier.
-                    if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
+                    if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
                     else __syncwarp();
                     if (lane == 0) {
                         ptx::mbar_arrive(bar_addr(bar_tempty, b));
@@ -803,7 +820,13 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             }
             __syncwarp();
             if (lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
-            if (tp) tp_finish(p, epoch, unit, q, lane, nb, mrow, row_ok);
+            if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
+        }
+        for (uint64_t todo = owned; todo; todo &= todo - 1) {
+            const int s = __ffsll(static_cast<long long>(todo)) - 1;
+            const int unit = unit0 + s, rb = unit % rbs;
+            const int mrow = rb * 128 + lane_row(row);
+            tp_collect(p, epoch, unit, q, lane, unit / rbs, mrow, mrow < p.m);
         }
     }
 
@@ -1208,6 +1231,13 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.resident = sched.grid <= d.sms ? 1 : 0;
     p.reducer_wait_ns = g_reducer_wait_ns.load(std::memory_order_relaxed);
     if (tp && tp->world > 1) {
+        // A CTA keeps the segments it must collect in a 64-bit mask.
+        const int per_cta = (sched.steps + sched.grid - 1) / sched.grid;
+        if (per_cta / kt + 2 > 64) {
+            zs_set_error("zipserv_mm_allreduce: more than 64 output segments per CTA (K/64 too "
+                         "small for this M and N)");
+            return cudaErrorInvalidValue;
+        }
         p.tp_world = tp->world, p.tp_rank = tp->rank;
         for (int r = 0; r < tp->world; ++r) {
             p.tp_recv[r] = static_cast<float*>(tp->recv[r]);
