@@ -539,7 +539,7 @@ def _reference_gpu_per_call(calls, stream, dev, settle) -> tuple[dict, str]:
 
     lib = _reference_bridge("libzipserv_ref_cuda.so")
     if lib is None or not hasattr(lib, "zipserv_mm"):
-        return {}, "the reference CUDA bridge is not built (make -C oracle ref-cuda)"
+        return {}, "the reference CUDA bridge is not built (make -C oracle ref-cuda REF=<reference checkout>)"
     ws = torch.empty(max(8 * c["n"] * c["lay"]["m"] for c in calls), dtype=torch.bfloat16,
                      device=dev)
     outs = [torch.empty_like(c["out"]) for c in calls]

@@ -179,11 +179,13 @@ int zipserv_pack_device_encode(void* stream, const void* weights, int m, int k,
  * Each rank passes its K shard of W and x; every rank receives the full
  * y = sum over ranks. When a CTA holds the final FP32 value of a 32-row x
  * bn-column piece it stores it into every rank's receive buffer (peer
- * stores over NVLink), raises its flag on every rank, waits (bounded) for
- * the other ranks' flags, sums the ranks' values in rank order (so every
- * rank stores identical BF16 outputs) and stores y. recv[r] / flags[r] are
- * rank r's receive buffer and flag array as this process maps them (its own
- * at index rank; the others opened through zipserv_ipc_open), each at least
+ * stores over NVLink; every value is one 64-bit word tagged with the launch
+ * number, so no fence or flag is needed), then waits (bounded) until every
+ * rank's values of its pieces carry this launch's tag, sums them in rank
+ * order (so every rank stores identical BF16 outputs) and stores y.
+ * recv[r] / flags[r] are rank r's receive buffer and flag area (reserved:
+ * 16 bytes, unused by this version) as this process maps them (its own at
+ * index rank; the others opened through zipserv_ipc_open), each at least
  * the sizes zipserv_mm_allreduce_sizes reports and zero-filled before first
  * use; `state` is this rank's 16-byte, zero-filled launch counter, advanced
  * by the kernel (so CUDA graphs may capture the call). Every rank must make

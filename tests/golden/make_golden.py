@@ -18,6 +18,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -78,7 +79,10 @@ def record(shim, words, m, k, base, small, legacy: bool):
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--ref", default="/root/reference")
+    parser.add_argument("--ref", default=os.environ.get("ZIPSERV_REFERENCE") or
+                        str(ROOT.parent / "reference"),
+                        help="reference checkout (default: ZIPSERV_REFERENCE, else a "
+                             "`reference` directory beside this repository)")
     args = parser.parse_args()
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "all", "ref", f"REF={args.ref}"],
                    check=True)

@@ -148,13 +148,14 @@ def test_l_api_header_declares_reference_entry_points():
 
 def test_fused_allreduce_sizes_and_argument_checks(native_lib):
     """zipserv_mm_allreduce_sizes: receive buffer = 2 parities x world x the
-    [N tile x 128] FP32 pieces of every unit; flags = 2 x world x units x 4
-    quarters. Invalid worlds and exchanges are refused before any GPU work."""
+    [N tile x 128] values of every unit, one 64-bit word each (FP32 value and
+    launch tag); the flag area is reserved (16 bytes). Invalid worlds and
+    exchanges are refused before any GPU work."""
     rb, fb = ctypes.c_uint64(0), ctypes.c_uint64(0)
     assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 2, ctypes.byref(rb), ctypes.byref(fb)) == 0
     units = 4096 // 128
-    assert rb.value == 2 * 2 * units * 16 * 128 * 4
-    assert fb.value == 2 * 2 * units * 4 * 4
+    assert rb.value == 2 * 2 * units * 16 * 128 * 8
+    assert fb.value == 16
     assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 1, ctypes.byref(rb), ctypes.byref(fb)) == 1
     assert native_lib.zipserv_mm_allreduce_sizes(4096, 16, 9, ctypes.byref(rb), ctypes.byref(fb)) == 1
     bufs = [None] * 7

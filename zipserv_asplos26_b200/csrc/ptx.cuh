@@ -104,6 +104,16 @@ __device__ __forceinline__ void stg_cg_f4(float* p, float4 v) {
                  "f"(v.z), "f"(v.w)
                  : "memory");
 }
+// Volatile (relaxed, system scope) 16-byte store and load of two 64-bit
+// words, for data exchanged with other GPUs without fences: each naturally
+// aligned 64-bit element is written and read whole, so a word that carries
+// its own flag is either entirely old or entirely new.
+__device__ __forceinline__ void st_volatile_v2u64(uint64_t* p, uint64_t a, uint64_t b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_volatile_v2u64(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
 __device__ __forceinline__ float4 ldg_cg_f4(const float* p) {
     float4 v;
     asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"

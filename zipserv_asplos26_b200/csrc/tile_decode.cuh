@@ -102,6 +102,13 @@ struct TileDecoder {
         const uint32_t rofs = min(uint32_t(max(med.y, 0)) + ord64 - before, cap_r);
         uint32_t co = common + cofs;
         const uint32_t arow_s = atile + arow;
+        if (!valid) {  // only in a ragged last row block: zero rows, no patches
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                ptx::sts128(arow_s + uint32_t(r) * 128u + (jx ^ (uint32_t(r) << 4)),
+                            make_uint4(0u, 0u, 0u, 0u));
+            return;
+        }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const uint32_t sel = 0x4440u | uint32_t(r & 3);
@@ -138,13 +145,12 @@ struct TileDecoder {
                 out[2] = __byte_perm(a, b, 0x5140);
                 out[3] = __byte_perm(a, b, 0x7362);
             }
-            if (!valid) out[0] = out[1] = out[2] = out[3] = 0u;
             ptx::sts128(arow_s + uint32_t(r) * 128u + (jx ^ (uint32_t(r) << 4)),
                         make_uint4(out[0], out[1], out[2], out[3]));
         }
         // Rare elements in row order: element p = 8r + c of the small tile is
         // the next word of the tile's rare run.
-        uint32_t rlo = valid ? ~ind_lo : 0u, rhi = valid ? ~ind_hi : 0u;
+        uint32_t rlo = ~ind_lo, rhi = ~ind_hi;
         uint32_t ri = rofs;
         const uint32_t rcap = cap_r ? cap_r - 1 : 0;
         while (rlo | rhi) {

@@ -9,21 +9,21 @@
 //               elected lane) with both operands in shared memory (A = a
 //               decoder group's tile of decoded W, B = an x tile, both
 //               128-byte swizzled) and two FP32 accumulators in TMEM;
-//   warps 1..   NDG decoder groups of four warps. Group g decodes K slices
-//               g, g+NDG, ... from two compressed slots it owns: while it
-//               decodes one, the other is filling. Warp w decodes 16-row
-//               band w%4 of both tiles (row = tile*64 + 16*band + i, tile
-//               row = 32*band + 16*tile + i); each thread rebuilds one W row
-//               (64 BF16) per slice in registers, writes it into the group's
-//               A tile with eight 16-byte stores and patches its rare
-//               elements with 16-bit stores; the groups also drain the
-//               accumulators (epilogue);
-//   next warp   keeps an x ring of nx slices filled with 3-D TMA loads;
-//   last two    producers: fill the groups' slots as soon as a group releases
-//               one, with few, large copies (an SM's copy engine takes ~100
-//               cycles per copy whatever its size): one 4-D tensor load for
-//               the three bitmap planes of both tile rows, one 3-D load for
-//               the band offsets, one bulk copy per payload run.
+//   warp 1      keeps a ring of x slices filled with 3-D TMA loads;
+//   warps 2-3   producers: fill the compressed ring's slots as soon as their
+//               previous K slice was decoded, with few, large copies (an
+//               SM's copy engine takes ~100 cycles per copy whatever its
+//               size): one 4-D tensor load for the three bitmap planes of
+//               both tile rows, one 3-D load for the band offsets, one bulk
+//               copy per payload run;
+//   warps 4..   NDG decoder groups of four warps. Group g decodes the CTA's
+//               K slices g, g+NDG, ... (slice t from ring entry t % nslots)
+//               into its A tile: warp q takes 16-row band q of both tiles,
+//               each thread rebuilds one 8x8 small tile (tile_decode.cuh)
+//               with 16-byte stores and patches its rare elements with
+//               16-bit stores;
+//   last 4      epilogue, one TMEM lane quarter each: TMEM -> BF16 -> y for
+//               whole units, TMEM -> FP32 pieces for split ones.
 // Split-K: the grid is persistent (one CTA per SM) and every CTA takes an
 // equal contiguous range of the (row block, K slice) work items, so each
 // gets the same amount of decoding whatever the shape. A row block whose K
@@ -95,9 +95,10 @@ __device__ __forceinline__ uint32_t bar_addr(uint32_t base, int index) {
 // runs in K order - a fixed order, so results do not depend on timing - and
 // the reducer returns the counter to zero.
 // The items are dealt out in groups of S consecutive K slices of one unit
-// (S = 2 when K/64 is even, else 1), so a CTA's range always holds whole
-// groups and each compressed slot carries one group: CTA c owns groups
-// [c * G / grid, (c + 1) * G / grid), G = steps / S.
+// (the host schedule uses S = 1; the kernel accepts any S dividing K/64),
+// so a CTA's range always holds whole groups and each compressed slot
+// carries one group: CTA c owns groups [c * G / grid, (c + 1) * G / grid),
+// G = steps / S.
 __device__ __forceinline__ int sched_start(int c, int grid, int groups, int S) {
     return S * int(int64_t(c) * groups / grid);
 }
@@ -114,75 +115,96 @@ __device__ __forceinline__ int step_owner(int item, const GemmParams& p) {
 // ----------------------------------------------------------------------
 // Fused all-reduce of the output (row-parallel layers over tp_world GPUs).
 // When a CTA holds the final FP32 value of a (unit, TMEM lane quarter) - a
-// whole unit, or a split unit it reduced - it sends the quarter's chunks to
-// every rank's receive buffer (peer stores over NVLink), raises its flag on
-// every rank, waits (bounded) for every rank's flag, sums the ranks' values
-// in rank order and stores BF16. Every rank runs the same schedule on its
-// K shard, so every rank computes every unit; the sum order is fixed, so all
-// ranks store identical outputs. Buffers are double-buffered by the launch's
-// epoch parity: a rank can be at most one launch ahead of another (it cannot
-// finish a launch without every rank's values), so the buffer it writes is
-// never the one a slower rank still reads.
-//   receive buffer: [2][world][units][4 quarters][chunks][32 lanes][16] FP32
-//   flags:          [2][world][units][4] u32 = epoch of the writing launch
+// whole unit, or a split unit it reduced - it stores the quarter's chunks
+// into every rank's receive buffer (peer stores over NVLink). After its last
+// segment it waits (bounded) for every rank's values of the units it holds,
+// sums them in rank order and stores BF16. Every rank runs the same schedule
+// on its K shard, so every rank computes every unit; the sum order is fixed,
+// so all ranks store identical outputs.
+// Each value travels as one 64-bit word (launch epoch << 32 | FP32 bits),
+// written and read whole: a reader knows a value has arrived when its word
+// carries this launch's epoch, so no fence or separate flag is needed (a
+// system-scope fence before a flag cost several microseconds per launch).
+// Buffers are double-buffered by the epoch's parity: a rank can be at most
+// one launch ahead of another (it cannot finish a launch without every
+// rank's values), so the buffer it writes is never the one a slower rank
+// still reads, and a word left from two launches ago carries another epoch.
+//   receive buffer: [2][world][units][4 quarters][chunks][8][32 lanes][2] u64
+// A chunk is a lane's 16 columns; columns 2i, 2i+1 sit in the chunk's i-th
+// 512-byte run, so every warp-wide 16-byte store or load covers 512
+// contiguous bytes (whole 128-byte lines across NVLink).
 __device__ __forceinline__ size_t tp_recv_index(const GemmParams& p, uint32_t par, int src,
                                                 int unit, int q, int c, int lane) {
     return ((((size_t(par) * p.tp_world + src) * p.units + unit) * 4 + q) * size_t(p.bn / 16) +
-            c) * 512u + size_t(lane) * 16u;
-}
-__device__ __forceinline__ size_t tp_flag_index(const GemmParams& p, uint32_t par, int src,
-                                                int unit, int q) {
-    return ((size_t(par) * p.tp_world + src) * p.units + unit) * 4 + q;
+            c) * 512u + size_t(lane) * 2u;
 }
 // This launch's epoch (read after the previous launch completed: every rank
-// counts its fused launches alike).
+// counts its fused launches alike; never 0, the buffers' initial contents).
 __device__ __forceinline__ uint32_t tp_epoch(const GemmParams& p) {
-    return *reinterpret_cast<volatile uint32_t*>(p.tp_state) + 1u;
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(p.tp_state) + 1u;
+    return e ? e : 1u;
+}
+__device__ __forceinline__ uint64_t tp_word(uint32_t epoch, float v) {
+    return (uint64_t(epoch) << 32) | __float_as_uint(v);
 }
 __device__ __forceinline__ void tp_put(const GemmParams& p, uint32_t epoch, int unit, int q, int c,
                                        int lane, const float (&acc)[16]) {
     for (int r = 0; r < p.tp_world; ++r) {
-        float* dst = p.tp_recv[r] + tp_recv_index(p, epoch & 1u, p.tp_rank, unit, q, c, lane);
+        uint64_t* dst = p.tp_recv[r] + tp_recv_index(p, epoch & 1u, p.tp_rank, unit, q, c, lane);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            ptx::stg_cg_f4(dst + 4 * i, make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2],
-                                                    acc[4 * i + 3]));
+        for (int i = 0; i < 8; ++i)
+            ptx::st_volatile_v2u64(dst + 64 * i, tp_word(epoch, acc[2 * i]),
+                                   tp_word(epoch, acc[2 * i + 1]));
     }
 }
-// Every chunk of (unit, q) has been put by this CTA (its warps met at a
-// barrier, or one warp put them all): raise this rank's flag on every rank.
-__device__ __forceinline__ void tp_publish(const GemmParams& p, uint32_t epoch, int unit, int q,
-                                           int lane) {
-    __threadfence_system();
-    __syncwarp();
-    if (lane < p.tp_world)
-        ptx::st_release_sys(p.tp_flags[lane] + tp_flag_index(p, epoch & 1u, p.tp_rank, unit, q),
-                            epoch);
-}
-// Wait (bounded) for every rank's pieces of (unit, q), sum them in rank
-// order and store BF16. Called once the CTA has published all its units, so
-// the wait overlaps the other ranks' remaining work rather than this one's.
+// Wait (bounded) for every rank's values of (unit, q), sum them in rank
+// order and store BF16. Called once the CTA has sent all its units, so the
+// wait overlaps the other ranks' remaining work rather than this one's.
 __device__ __noinline__ void tp_collect(const GemmParams& p, uint32_t epoch, int unit, int q,
                                         int lane, int nb, int mrow, bool row_ok) {
     const uint32_t par = epoch & 1u;
+    const uint64_t* mine = p.tp_recv[p.tp_rank];
     bool ok = true;
-    if (lane < p.tp_world)
-        ok = ptx::wait_global_eq_sys(p.tp_flags[p.tp_rank] + tp_flag_index(p, par, lane, unit, q),
-                                     epoch, 2000000000ull);
-    ok = __all_sync(kFullMask, ok);
-    const float* mine = p.tp_recv[p.tp_rank];
     for (int c = 0; c < p.bn / 16; ++c) {
         float acc[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-        for (int src = 0; src < p.tp_world; ++src) {
-            const float* from = mine + tp_recv_index(p, par, src, unit, q, c, lane);
+        // Two ranks' values per polling round (one round trip for TP 2):
+        // acc += (value of rank src + value of rank src + 1), src = 0, 2, ...
+        // - a fixed order, the same on every rank.
+        for (int src = 0; src < p.tp_world; src += 2) {
+            const bool two = src + 1 < p.tp_world;
+            const uint64_t* f0 = mine + tp_recv_index(p, par, src, unit, q, c, lane);
+            const uint64_t* f1 = two ? mine + tp_recv_index(p, par, src + 1, unit, q, c, lane) : f0;
+            float t[16];
+            uint64_t t0 = 0;
+            for (uint32_t it = 0;; ++it) {
+                uint32_t mismatch = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float4 v = ptx::ldg_cg_f4(from + 4 * i);
-                acc[4 * i] += v.x, acc[4 * i + 1] += v.y, acc[4 * i + 2] += v.z,
-                    acc[4 * i + 3] += v.w;
+                for (int i = 0; i < 8; ++i) {
+                    uint64_t a0, a1, b0, b1;
+                    ptx::ld_volatile_v2u64(f0 + 64 * i, a0, a1);
+                    ptx::ld_volatile_v2u64(f1 + 64 * i, b0, b1);
+                    mismatch |= (uint32_t(a0 >> 32) ^ epoch) | (uint32_t(a1 >> 32) ^ epoch) |
+                                (uint32_t(b0 >> 32) ^ epoch) | (uint32_t(b1 >> 32) ^ epoch);
+                    t[2 * i] = __uint_as_float(uint32_t(a0)) +
+                               (two ? __uint_as_float(uint32_t(b0)) : 0.f);
+                    t[2 * i + 1] = __uint_as_float(uint32_t(a1)) +
+                                   (two ? __uint_as_float(uint32_t(b1)) : 0.f);
+                }
+                if (!mismatch || !ok) break;
+                if ((it & 15) == 15) {
+                    const uint64_t now = ptx::global_timer_ns();
+                    if (!t0) t0 = now;
+                    else if (now - t0 > 2000000000ull) {
+                        atomicOr(&g_device_flags, 1u);
+                        ok = false;
+                    }
+                    __nanosleep(64);
+                }
             }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] += t[j];
         }
         if (!row_ok || !ok) continue;
 #pragma unroll
@@ -282,17 +304,17 @@ __device__ __noinline__ void help_reduce(const GemmParams* gp, float* ws_partial
                          cta, parts, unit / rbs, mrow, lane, size_t(q) * size_t(chunks),
                          mrow < m, dok, true, gp, epoch, unit, q};
     for (int c = g + 1; c < chunks; c += stride) cr.run(c);
-    // Chunks sent to other GPUs are ordered before the epilogue warp's flags.
-    if (gp->tp_world > 1) __threadfence_system();
+    // Chunks sent to other GPUs: the named barrier below orders them before
+    // the epilogue warp's system-scope release of the flags.
     ptx::tc_fence_before();
 }
 
 // Warp roles: warp 0 allocates TMEM and issues the MMAs; warp 1 keeps the x
 // ring filled; warps 2-3 fill the decoder groups' compressed slots; warps
 // 4 .. 4 + 4*NDG - 1 form NDG decoder groups (local step t, item
-// start(c) + t, is decoded by group t % NDG from its slot 2*group +
-// ((t / NDG) & 1)); the last four warps drain the accumulators (epilogue),
-// one TMEM lane quarter each.
+// start(c) + t, is decoded by group t % NDG from ring entry (t / S) %
+// nslots); the last four warps drain the accumulators (epilogue), one TMEM
+// lane quarter each.
 template <int NDG>
 __global__ void __launch_bounds__(256 + 128 * NDG, 1)
     zipgemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ PlaneMaps pm,
@@ -488,9 +510,10 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         // band offsets, one bulk copy per payload stream and tile row (the S
         // tiles of a tile row are consecutive in the packed streams), and the
         // tile-relative payload starts written into the slot header. An SM
-        // takes ~100 cycles per copy whatever its size, so S = 2 halves the
-        // copies per K slice. The packed weight is never written by other
-        // kernels: no prerequisite wait.
+        // takes ~100 cycles per copy whatever its size (S > 1 would halve the
+        // copies per K slice; it measured no faster, so the host uses S = 1).
+        // The packed weight is never written by other kernels: no
+        // prerequisite wait.
         const int pi = warp - 2;
         const uint64_t pol_w = ptx::policy_evict_first();
         const int S = p.S, nslots = p.nslots;
@@ -715,7 +738,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(bar_addr(bar_tempty, b));
-                if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
+                if (tp) owned |= 1ull << (s & 63);
                 continue;
             }
             // Partial segments are a CTA's first or last: slot `which`.
@@ -755,9 +778,8 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                     for (int c = 0; c < chunks; c += stride) cr.run(c);
                     ptx::tc_fence_before();
                     if (chunks > 1) ptx::named_barrier_sync(1u + uint32_t(q), 32u * (1u + NDG));
-                    // The helpers' chunks were sent before the barrier.
-                    if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
-                    else __syncwarp();
+                    if (tp) owned |= 1ull << (s & 63);
+                    __syncwarp();
                     if (lane == 0) {
                         ptx::mbar_arrive(bar_addr(bar_tempty, b));
                         *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
@@ -820,7 +842,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             }
             __syncwarp();
             if (lane == 0) *reinterpret_cast<volatile uint32_t*>(ctr) = 0u;  // ready for reuse
-            if (tp) tp_publish(p, epoch, unit, q, lane), owned |= 1ull << (s & 63);
+            if (tp) owned |= 1ull << (s & 63);
         }
         for (uint64_t todo = owned; todo; todo &= todo - 1) {
             const int s = __ffsll(static_cast<long long>(todo)) - 1;
@@ -1181,8 +1203,8 @@ void allreduce_exchange_bytes(int m, int n, int world, size_t* recv_bytes, size_
     *recv_bytes = *flag_bytes = 0;
     if (!valid_matrix(m, 64) || n <= 0 || world < 2 || world > kMaxTp) return;
     const Schedule s = make_schedule(m, n, 64, 0, 1);  // units and N tile do not depend on K
-    *recv_bytes = size_t(2) * world * s.units * s.bn * 128u * sizeof(float);
-    *flag_bytes = (size_t(2) * world * s.units * 4u * sizeof(uint32_t) + 15u) / 16u * 16u;
+    *recv_bytes = size_t(2) * world * s.units * s.bn * 128u * sizeof(uint64_t);
+    *flag_bytes = 16;  // reserved: values carry their own epoch
 }
 
 int plan_kparts(int m, int n, int k, int device) {
@@ -1240,8 +1262,7 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
         }
         p.tp_world = tp->world, p.tp_rank = tp->rank;
         for (int r = 0; r < tp->world; ++r) {
-            p.tp_recv[r] = static_cast<float*>(tp->recv[r]);
-            p.tp_flags[r] = static_cast<uint32_t*>(tp->flags[r]);
+            p.tp_recv[r] = static_cast<uint64_t*>(tp->recv[r]);
         }
         p.tp_state = static_cast<uint32_t*>(tp->state);
     }

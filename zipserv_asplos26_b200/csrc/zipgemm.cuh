@@ -66,12 +66,11 @@ struct GemmParams {
     uint32_t tmem_cols;    // columns of one accumulator (two are allocated)
     uint64_t reducer_wait_ns;  // how long a row block's first part waits for the others
     // Fused all-reduce of the output over tp_world ranks (row-parallel
-    // layers; tp_world <= 1: off). tp_recv[r] / tp_flags[r] are rank r's
-    // receive buffer and flags as this GPU addresses them (peer memory);
-    // tp_state is this rank's [epoch, finished CTAs] pair.
+    // layers; tp_world <= 1: off). tp_recv[r] is rank r's receive buffer as
+    // this GPU addresses it (peer memory); tp_state is this rank's [epoch,
+    // finished CTAs] pair.
     int tp_world, tp_rank;
-    float* tp_recv[kMaxTp];
-    uint32_t* tp_flags[kMaxTp];
+    uint64_t* tp_recv[kMaxTp];
     uint32_t* tp_state;
 };
 
@@ -120,7 +119,8 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
                            const TpExchange* tp = nullptr);
 int plan_kparts(int m, int n, int k, int device);
 // Fused all-reduce exchange of one launch: the peers' receive buffers and
-// flags (index = rank) and this rank's state pair; sizes checked by the caller.
+// flag areas (index = rank; the flag areas are reserved, values carry their
+// own epoch) and this rank's state pair; sizes checked by the caller.
 struct TpExchange {
     int world, rank;
     void* const* recv;
