@@ -169,28 +169,19 @@ __device__ __noinline__ void tp_collect(const GemmParams& p, uint32_t epoch, int
         float acc[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = 0.f;
-        // Two ranks' values per polling round (one round trip for TP 2):
-        // acc += (value of rank src + value of rank src + 1), src = 0, 2, ...
-        // - a fixed order, the same on every rank.
-        for (int src = 0; src < p.tp_world; src += 2) {
-            const bool two = src + 1 < p.tp_world;
-            const uint64_t* f0 = mine + tp_recv_index(p, par, src, unit, q, c, lane);
-            const uint64_t* f1 = two ? mine + tp_recv_index(p, par, src + 1, unit, q, c, lane) : f0;
-            float t[16];
+        for (int src = 0; src < p.tp_world; ++src) {
+            const uint64_t* from = mine + tp_recv_index(p, par, src, unit, q, c, lane);
+            float v[16];
             uint64_t t0 = 0;
             for (uint32_t it = 0;; ++it) {
                 uint32_t mismatch = 0;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    uint64_t a0, a1, b0, b1;
-                    ptx::ld_volatile_v2u64(f0 + 64 * i, a0, a1);
-                    ptx::ld_volatile_v2u64(f1 + 64 * i, b0, b1);
-                    mismatch |= (uint32_t(a0 >> 32) ^ epoch) | (uint32_t(a1 >> 32) ^ epoch) |
-                                (uint32_t(b0 >> 32) ^ epoch) | (uint32_t(b1 >> 32) ^ epoch);
-                    t[2 * i] = __uint_as_float(uint32_t(a0)) +
-                               (two ? __uint_as_float(uint32_t(b0)) : 0.f);
-                    t[2 * i + 1] = __uint_as_float(uint32_t(a1)) +
-                                   (two ? __uint_as_float(uint32_t(b1)) : 0.f);
+                    uint64_t a0, a1;
+                    ptx::ld_volatile_v2u64(from + 64 * i, a0, a1);
+                    mismatch |= (uint32_t(a0 >> 32) ^ epoch) | (uint32_t(a1 >> 32) ^ epoch);
+                    v[2 * i] = __uint_as_float(uint32_t(a0));
+                    v[2 * i + 1] = __uint_as_float(uint32_t(a1));
                 }
                 if (!mismatch || !ok) break;
                 if ((it & 15) == 15) {
@@ -204,7 +195,7 @@ __device__ __noinline__ void tp_collect(const GemmParams& p, uint32_t epoch, int
                 }
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] += t[j];
+            for (int j = 0; j < 16; ++j) acc[j] += v[j];
         }
         if (!row_ok || !ok) continue;
 #pragma unroll
