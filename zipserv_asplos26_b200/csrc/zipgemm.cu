@@ -962,7 +962,13 @@ SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r
     // separate tensor loads require). Then the tiles' band offsets (32 B
     // each), a header of tile-relative payload starts ([2][S] int2, written
     // by the producer), and per tile row one common and one rare run of its S
-    // tiles (the row-1 runs 64 bytes further modulo 128).
+    // tiles. The row-1 common run starts 32 bytes further modulo 128: a
+    // warp's lanes read the small tiles of one band of both tiles, whose
+    // runs sit ~62 bytes apart, so within a tile they spread over the banks
+    // in two interleaved combs ~half a bank row apart; a 32-byte shift puts
+    // the other tile's lanes between them (64 would put them on the same
+    // banks). Modelled on N(0, 0.02) weights: 3.2 instead of 4.3 shared
+    // wavefronts per payload load.
     SlotLayout s{};
     const uint32_t us = uint32_t(S);
     s.plane1 = plane_pitch;
@@ -970,7 +976,7 @@ SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r
     s.med = round_up(3u * s.plane_stride, 128);  // [2S][32 B]
     s.hdr = s.med + 64u * us;                    // [2S] int2
     s.common0 = round_up(s.hdr + 16u * us, 128);
-    s.common1 = s.common0 + us * cap_c + 64;  // cap_c is a multiple of 128
+    s.common1 = s.common0 + us * cap_c + 32;  // cap_c is a multiple of 128
     s.rare0 = round_up(s.common1 + us * cap_c, 16);
     s.rare1 = s.rare0 + us * cap_r * 2;
     s.bytes = round_up(s.rare1 + us * cap_r * 2, 128);
