@@ -2,11 +2,11 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE configs[1]): the four Llama-3-8B linears, qkv 6144x4096,
+Workload: the four Llama-3-8B linears, qkv 6144x4096,
 o 4096x4096, gate_up 28672x4096 and down 4096x14336, weights ~N(0, 0.02) BF16
 packed to TCA-TBE, activations ~N(0, 1) BF16 with N in {1, 8, 16, 32, 64, 128}
 tokens. One step = the 24 fused ZipGEMM calls (4 linears x 6 token counts).
-The metric is BASELINE's: ZipGEMM HBM GB/s on compressed bytes, i.e.
+The metric: ZipGEMM HBM GB/s on compressed bytes, i.e.
 algorithmic bytes (packed weight + activations + BF16 output) / time.
 
 Timing: every call has its own device copy of its weight, so one step
@@ -697,7 +697,7 @@ def run_reference(args, world: int, rank: int) -> dict | None:
 
 
 def decode_step_case(args, world: int, rank: int, dev) -> dict:
-    """one greedy decode step of a random-init
+    """The Llama-3-8B decode step: one greedy decode step of a random-init
     Llama-3-8B (32 layers, 2048 cached positions per sequence, untied
     compressed lm_head) at TP = world, every linear through ZipGEMM, against
     the same step with the dense BF16 weights (cuBLAS). Each step is a CUDA
@@ -757,7 +757,7 @@ def decode_step_case(args, world: int, rank: int, dev) -> dict:
     return out
 
 
-LLAMA70B = (  # name, M, K, tensor-parallel split (BASELINE configs[3])
+LLAMA70B = (  # name, M, K, tensor-parallel split
     ("qkv", 10240, 8192, "col"),
     ("o", 8192, 8192, "row"),
     ("gate_up", 57344, 8192, "col"),
@@ -766,7 +766,7 @@ LLAMA70B = (  # name, M, K, tensor-parallel split
 
 
 def tp70b_case(args, world: int, rank: int, dev) -> dict:
-    """the Llama-3-70B linears split over `world` GPUs
+    """The Llama-3-70B shape table: the Llama-3-70B linears split over `world` GPUs
     (qkv and gate_up on output rows, o and down on K), N in {1, 16, 64, 256}.
     Per call, after a 256 MiB L2 flush: ZipGEMM and cuBLAS BF16 on this
     rank's shard, and for the row-parallel layers the NCCL all-reduce of the
@@ -791,6 +791,7 @@ def tp70b_case(args, world: int, rank: int, dev) -> dict:
         ts = []
         for _ in range(5):
             flush.zero_()
+            torch.cuda._sleep(1_000_000)  # the host enqueues fn meanwhile: device time only
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()
@@ -830,7 +831,7 @@ def tp70b_case(args, world: int, rank: int, dev) -> dict:
     if flags:
         raise SystemExit(f"device failure flags {flags:#x} set during the 70B case")
     return {"workload": "llama3-70b linears, tp%d shards, N in {1,16,64,256}" % world,
-            "timing": "median of 5 per-call CUDA events after a 256 MiB L2 flush, max over ranks",
+            "timing": "median of 5 per-call CUDA events after a 256 MiB L2 flush (the call enqueued behind a GPU sleep, so host launch time is excluded), max over ranks",
             "per_shape": rows}
 
 
@@ -852,6 +853,7 @@ def threshold_sweep(args) -> None:
         ts = []
         for _ in range(7):
             flush.zero_()
+            torch.cuda._sleep(1_000_000)  # the host enqueues fn meanwhile: device time only
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()
@@ -882,7 +884,7 @@ def threshold_sweep(args) -> None:
 
 
 def stress_case(args) -> dict:
-    """BASELINE configs[2] on this GPU: a 28672x8192 weight with 5 % N(0, 1)
+    """The exception-stress configuration on this GPU: a 28672x8192 weight with 5 % N(0, 1)
     outliers. Standalone decompression (algorithmic bytes = packed + dense
     output), the fused path at N = 16, and prefill at N = 4096 as
     decompression + cuBLAS BF16 against cuBLAS on the dense weight. Every
@@ -912,6 +914,7 @@ def stress_case(args) -> dict:
         times = []
         for _ in range(reps):
             flush.zero_()
+            torch.cuda._sleep(1_000_000)  # the host enqueues fn meanwhile: device time only
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
             fn()
@@ -939,7 +942,7 @@ def stress_case(args) -> dict:
         "prefill_n4096_decompress_plus_cublas_us": round(t_prefill, 1),
         "prefill_n4096_cublas_dense_us": round(t_dense, 1),
         "prefill_tflops": round(2 * m * k * 4096 / (t_prefill * 1e-6) / 1e12, 1),
-        "timing": "median of per-call CUDA events after a 256 MiB L2 flush",
+        "timing": "median of per-call CUDA events after a 256 MiB L2 flush (the call enqueued behind a GPU sleep, so host launch time is excluded)",
     }
 
 

@@ -123,7 +123,7 @@ def main() -> None:
     gap[120] = gap[126] = 10000
 
     # The C-ABI bridge's own output for the CPU round-trip configuration
-    # 4096x4096 N(0,0.02) seed 0.
+    # (the CPU-runnable configuration): 4096x4096 N(0,0.02) seed 0.
     bridge = ctypes.CDLL(str(ROOT / "oracle/_ref/libzipserv_ref_cpu.so"))
     bridge.zipserv_compress.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                         ctypes.POINTER(NativePacked)]

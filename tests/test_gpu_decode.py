@@ -1,7 +1,7 @@
 """Bit-exact GPU decompression (zipserv_decode through the C ABI) against the
 original words and the CPU oracle. Cases follow the reference's own tests:
 tests/test_cuda.cu:96-107 (all words and edge modes) and the encoder cases of
-tests/test_host_packer.cpp:69-111, plus BASELINE-sized weights."""
+tests/test_host_packer.cpp:69-111, plus benchmark-sized weights."""
 from __future__ import annotations
 
 import numpy as np

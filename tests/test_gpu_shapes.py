@@ -1,8 +1,8 @@
 """Fused ZipGEMM parity at the benchmarked and configured shapes.
 
-* The four Llama-3-8B linears at full size, including
+* The four Llama-3-8B linears at full size (the benchmark sweep), including
   gate_up 28672x4096 and down 4096x14336 whose K/64 = 224 gives the persistent
-  schedule different segment boundaries, and 4096x4096 at N = 8 (configs[0],
+  schedule different segment boundaries, and 4096x4096 at N = 8 (the CPU-runnable configuration,
   the reference's `test_mm 4096 4096 8 1` shape).
 * One row-parallel shard per tensor-parallel degree (o and down split on K
   at TP 2/4/8, the Llama-3-70B down shard K = 3584) and the 70B column shards.
@@ -78,8 +78,8 @@ def test_llama3_8b_linears_full_size(native_lib, oracle_mod, name, m, k):
 
 
 def test_config0_shape_against_cpu_oracle(native_lib, oracle_mod):
-    """4096 x 4096, N = 8, weights seed 0 and activations seed 1 as BASELINE
-    configs[0] states, against the CPU oracle's own FP32 GEMM."""
+    """4096 x 4096, N = 8, weights seed 0 and activations seed 1 (the
+    CPU-runnable configuration), against the CPU oracle's own FP32 GEMM."""
     m = k = 4096
     w = oracle_mod.llama_weight(m, k, seed=0)
     packed = runtime.compress(bf16_tensor(w)).to("cuda")

@@ -1,4 +1,4 @@
-"""Exception-stress configuration at full size (BASELINE configs[2]): a
+"""Exception-stress configuration at full size: a
 28672x8192 BF16 weight, 95 % N(0, 0.02) and 5 % N(0, 1) outliers at seeded
 uniform positions. Checked through size-independent properties, since the
 CPU oracle is too slow at this size:

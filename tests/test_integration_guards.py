@@ -43,7 +43,7 @@ def test_startup_and_decode_budget_rejections():
 
 
 def test_per_shape_threshold():
-    """with per_shape_threshold each layer is also capped at its
+    """With per_shape_threshold each layer is also capped at its
     measured B200 crossover, smaller weights switching to decompression +
     stock GEMM at fewer tokens."""
     limits = [policy.b200_token_limit(m, k) for m, k in

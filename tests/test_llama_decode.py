@@ -1,5 +1,5 @@
 """The Llama-3 decode-step workload (zipserv_asplos26_b200.llama_decode, the
-model of BASELINE configs[4]) at a reduced shape.
+benchmarked decode-step model) at a reduced shape.
 
 CPU (gloo, two ranks): the Megatron split of the step — qkv by heads,
 gate_up by intermediate rows, o and down on K with an all-reduce, the

@@ -38,15 +38,18 @@ STARTUP_SLICES = 3.0      # per-CTA fixed cost, in K-slice units (B200 measureme
 # CUDA-graph capture sizes within it.
 B200_LARGE_BATCH_TOKENS = 176
 
-# Per-weight crossover on a B200 (SURVEY f2): the first token count at which
+# Per-weight crossover on a B200: the first token count at which
 # decompression + cuBLAS BF16 beats the fused kernel, per weight size (M*K
 # elements), measured with per-call device time after an L2 flush
-# (bench.py --threshold-sweep). A weight above the last bound uses its value.
+# (bench.py --threshold-sweep; token counts 16 .. 768): Llama-3-8B o (16.8M)
+# crosses at 32, qkv (25.2M) at 128, down (58.7M) at 256, gate_up (117M) at
+# 384; Llama-3-70B TP-1 o (67.1M) at 256, qkv (83.9M), down and gate_up at
+# 384. A weight above the last bound uses its value.
 B200_CROSSOVER = (
-    (20_000_000, 64),
-    (40_000_000, 96),
-    (80_000_000, 192),
-    (float("inf"), 320),
+    (20_000_000, 32),
+    (40_000_000, 128),
+    (70_000_000, 256),
+    (float("inf"), 384),
 )
 
 

@@ -1,8 +1,8 @@
 """A random-initialised Llama-3 decode step whose linears run through ZipGEMM.
 
-The workload behind BASELINE configs[4] ("full decode step of a random-init
-Llama-3-8B architecture ... linears via ZipGEMM; per-step latency at
-TP = 1/2/4/8 against cuBLAS BF16"): 32 layers, hidden 4096, 32 query and 8
+The benchmarked decode step (a full decode step of a random-init
+Llama-3-8B architecture with its linears on ZipGEMM, per-step latency at
+TP = 1/2/4/8 against cuBLAS BF16): 32 layers, hidden 4096, 32 query and 8
 KV heads of dim 128, SwiGLU intermediate 14336, vocabulary 128256 with an
 untied, compressed lm_head, RMSNorm weights 1.0, every linear N(0, 0.02)
 BF16, and a KV cache of `context` random entries per sequence. One step
