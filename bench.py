@@ -73,6 +73,9 @@ def _config(args, world: int) -> dict:
               "(inputs larger than the 126 MB L2); calls run back to back between one "
               "pair of events per step",
         "parallelism": f"tp{world}" if world > 1 else "single",
+        **({"row_parallel_sum": "o and down split on K; their outputs summed inside the "
+                                "fused kernel up to 32 tokens, by the GEMM + an NCCL "
+                                "all-reduce above"} if world > 1 else {}),
     }
 
 
@@ -229,8 +232,10 @@ def run_ours(args, world: int, rank: int) -> dict | None:
 
     total_bytes = sum(call_bytes(c) for c in calls)
 
-    # Row-parallel layers sum their outputs across ranks inside the fused
-    # kernel (tp.PeerExchange); the NCCL all-reduce variant is timed beside it.
+    # Row-parallel layers sum their outputs across ranks through
+    # tp.PeerExchange: inside the fused kernel up to its token limit, else
+    # the GEMM and an NCCL all-reduce. The per-shape table also times both
+    # routes at every token count.
     exchange = None
     if need_reduce:
         from zipserv_asplos26_b200 import tp as tpmod
@@ -241,6 +246,11 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     def zip_call(c):
         if need_reduce and c["lay"]["split"] == "row":
             return exchange.linear(c["x"], c["packed"], out=c["out"])
+        return runtime.linear_kparts(c["x"], c["packed"], 0, out=c["out"])
+
+    def fused_call(c):
+        if need_reduce and c["lay"]["split"] == "row":
+            return exchange.linear(c["x"], c["packed"], out=c["out"], fused=True)
         return runtime.linear_kparts(c["x"], c["packed"], 0, out=c["out"])
 
     def zip_nccl_call(c):
@@ -314,11 +324,13 @@ def run_ours(args, world: int, rank: int) -> dict | None:
     per_call: dict = {}
     dense_per_call: dict = {}
     nccl_per_call: dict = {}
+    fused_per_call: dict = {}
     for _ in range(max(3, min(args.steps, 10))):
         per_call_pass(zip_call, per_call)
         per_call_pass(dense_call, dense_per_call)
         if need_reduce:
             per_call_pass(zip_nccl_call, nccl_per_call)
+            per_call_pass(fused_call, fused_per_call)
     barrier()
     ref_gpu, ref_gpu_note = (_reference_gpu_per_call(calls, stream, dev, settle)
                              if world == 1 else ({}, "single-GPU runs only"))
@@ -428,9 +440,10 @@ def run_ours(args, world: int, rank: int) -> dict | None:
                "zipgemm_us": round(us, 2), "cublas_bf16_us": round(dus, 2),
                "gbs": round(call_bytes(c) / (us * 1e-6) / 1e9, 1),
                "speedup_vs_cublas": round(dus / us, 3)}
-        if key in nccl_per_call:
+        if key in nccl_per_call and lay["split"] == "row":
             row["zipgemm_then_nccl_allreduce_us"] = round(
                 statistics.median(nccl_per_call[key]) * 1e3, 2)
+            row["fused_allreduce_us"] = round(statistics.median(fused_per_call[key]) * 1e3, 2)
         if key in ref_gpu:
             rus, rsplit = ref_gpu[key]
             row.update({"reference_gpu_us": round(rus, 2), "reference_split_k": rsplit,
@@ -440,7 +453,9 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         per_shape.append(row)
     traffic = _traffic_record()
     launches = len(calls) * steps
-    avg_launch_bytes = step_bytes / len(calls)
+    # Per GPU: every rank launches the same calls on its own shards.
+    avg_launch_bytes = step_bytes / world / len(calls)
+    per_gpu = value / world
     line = {
         "metric": METRIC,
         "value": round(value, 1),
@@ -458,10 +473,11 @@ def run_ours(args, world: int, rank: int) -> dict | None:
         "bytes_per_step": int(step_bytes),
         "roofline": {
             "bound": "hbm",
-            "achieved": round(value, 1),
+            "achieved": round(per_gpu, 1),
             "peak": peaks["hbm_gbs"],
             "unit": "GB/s",
-            "frac": round(value / peaks["hbm_gbs"], 4),
+            "frac": round(per_gpu / peaks["hbm_gbs"], 4),
+            "per": "one GPU (the job's algorithmic bytes per GPU over the step time)",
             "peak_source": peaks["source"],
             "traffic": (round(traffic["ratio"] * avg_launch_bytes)
                         if traffic.get("ratio") else None),
@@ -822,7 +838,7 @@ def tp70b_case(args, world: int, rank: int, dev) -> dict:
                 y = torch.empty(n, mm, dtype=torch.bfloat16, device=dev)
                 row["nccl_allreduce_us"] = round(timed(lambda: dist.all_reduce(y)), 2)
                 row["zipgemm_fused_allreduce_us"] = round(
-                    timed(lambda: exchange.linear(x, packed, out=y)), 2)
+                    timed(lambda: exchange.linear(x, packed, out=y, fused=True)), 2)
             rows.append(row)
         del packed, local
     if exchange is not None:

@@ -44,6 +44,7 @@ def _rank_main(rank, world, port, results):
 
     out = {"errors": [], "identical": True, "deterministic": True, "graph": True}
     exchange = tp.PeerExchange(4096, 128)
+    exchange.fused_max_tokens = 128  # the fused kernel at every tested token count
     try:
         for li, (name, m, k) in enumerate(SHAPES):
             g = torch.Generator().manual_seed(50 + li)
@@ -67,6 +68,12 @@ def _rank_main(rank, world, port, results):
                 torch.backends.cuda.matmul.allow_tf32 = prev
                 mx, mean = rel_errors(words_of(y), words_of(ref))
                 out["errors"].append((name, n, mx, mean))
+                # The other route (GEMM + NCCL all-reduce), as chosen above
+                # the default token limit.
+                c0, c1 = tp.shard_bounds(k, world, rank)
+                y2 = exchange.linear(x[..., c0:c1].contiguous(), layer.packed, fused=False)
+                mx, mean = rel_errors(words_of(y2), words_of(ref))
+                out["errors"].append((name + "+nccl", n, mx, mean))
             # CUDA graph of the fused call (shape never captured before).
             x = torch.randn(16, k, generator=torch.Generator().manual_seed(99)).to(
                 torch.bfloat16).cuda()
@@ -105,4 +112,9 @@ def test_fused_row_parallel_allreduce():
         assert out["flags"] == 0, rank
         assert out["identical"] and out["deterministic"] and out["graph"], (rank, out)
         for name, n, mx, mean in out["errors"]:
-            assert mx <= MAX_REL_TOL and mean <= MEAN_REL_TOL, (rank, name, n, mx, mean)
+            # The NCCL route sums BF16 partial outputs (each rank's GEMM rounds
+            # to BF16, then the all-reduce adds in BF16): three roundings where
+            # the fused kernel has one, so it gets three times the tolerance.
+            scale = 3.0 if name.endswith("+nccl") else 1.0
+            assert mx <= scale * MAX_REL_TOL and mean <= scale * MEAN_REL_TOL, (
+                rank, name, n, mx, mean)
