@@ -969,12 +969,24 @@ def run_profile_case(spec: str, repeats: int) -> None:
     from zipserv_asplos26_b200 import runtime
 
     name, n = spec.split(":")
+    if name == "decompress":  # decompress:<layer>: the standalone decode kernel
+        name, n = n, 0
     n = int(n)
     lay = {l[0]: l for l in LAYERS}[name]
     _, m, k, _ = lay
     g = torch.Generator().manual_seed(1000 + [l[0] for l in LAYERS].index(name))
     w = (torch.randn(m, k, generator=g) * 0.02).to(torch.bfloat16)
     packed = runtime.compress(w).to("cuda")
+    if n == 0:
+        out = torch.empty(m, k, dtype=torch.bfloat16, device="cuda")
+        for _ in range(repeats):
+            runtime.decompress(packed, out=out)
+        torch.cuda.synchronize()
+        if not torch.equal(out.cpu().view(torch.int16), w.view(torch.int16)):
+            raise SystemExit("decompression is not bit-exact")
+        print(json.dumps({"profile_case": spec, "m": m, "k": k, "repeats": repeats,
+                          "algorithmic_bytes_per_launch": packed.storage_bytes + 2 * m * k}))
+        return
     x = torch.randn(n, k, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).cuda()
     for _ in range(repeats):
         runtime.linear(x, packed)
@@ -994,7 +1006,9 @@ def main() -> None:
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--tokens", type=int, nargs="*", default=list(TOKENS))
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--profile", metavar="LAYER:N", help="run one linear for ncu, e.g. o:16")
+    parser.add_argument("--profile", metavar="LAYER:N",
+                        help="run one linear for ncu, e.g. o:16 (decompress:gate_up: the "
+                             "standalone decompression of that weight)")
     parser.add_argument("--repeats", type=int, default=4)
     parser.add_argument("--no-extras", action="store_true",
                         help="skip the Llama-3-70B TP shapes and the Llama-3-8B decode step")
