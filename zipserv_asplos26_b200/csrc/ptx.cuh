@@ -327,8 +327,11 @@ __device__ __forceinline__ void mma_bf16_ss_elect(uint32_t d_tmem, uint64_t a_de
 // One K slice of 64: four K = 16 MMAs (the first overwrites the accumulator
 // unless `accumulate`) and a commit to `bar`, all from one elected lane of a
 // converged warp. Descriptors are passed as their 32-bit halves: stepping
-// 16 K elements (32 bytes) adds 2 to the low half's start-address field,
-// which never carries out of it for shared-memory addresses.
+// 16 K elements adds AK to A's start-address field (16-byte units; 2 for a
+// 128-byte-swizzled operand, 2 * LBO / 16 without swizzle) and 2 to B's
+// (128-byte swizzled), which never carries out of the field for
+// shared-memory addresses.
+template <int AK>
 __device__ __forceinline__ void mma_bf16_slice_elect(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
                                                      uint32_t b_lo, uint32_t b_hi, uint32_t idesc,
                                                      uint32_t accumulate, uint32_t bar) {
@@ -342,24 +345,25 @@ __device__ __forceinline__ void mma_bf16_slice_elect(uint32_t d_tmem, uint32_t a
         "mov.b64 ad, {%1, %2};\n\t"
         "mov.b64 bd, {%3, %4};\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t"
-        "add.u32 al, %1, 2;\n\t"
+        "add.u32 al, %1, %8;\n\t"
         "add.u32 bl, %3, 2;\n\t"
         "mov.b64 ad, {al, %2};\n\t"
         "mov.b64 bd, {bl, %4};\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
-        "add.u32 al, %1, 4;\n\t"
+        "add.u32 al, %1, %9;\n\t"
         "add.u32 bl, %3, 4;\n\t"
         "mov.b64 ad, {al, %2};\n\t"
         "mov.b64 bd, {bl, %4};\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
-        "add.u32 al, %1, 6;\n\t"
+        "add.u32 al, %1, %10;\n\t"
         "add.u32 bl, %3, 6;\n\t"
         "mov.b64 ad, {al, %2};\n\t"
         "mov.b64 bd, {bl, %4};\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, q;\n\t"
         "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(
             d_tmem),
-        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(bar), "r"(accumulate)
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(bar), "r"(accumulate),
+        "n"(AK), "n"(2 * AK), "n"(3 * AK)
         : "memory");
 }
 // Commit from one elected lane of a converged warp (see mma_bf16_ss_elect).
@@ -385,6 +389,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16_m128(uint32_t n) {
 // Shared-memory matrix descriptor for a K-major operand stored in the
 // 128-byte-swizzled layout TMA writes for a 64-element (128 B) BF16 box
 // width: 8-row x 128 B atoms, atoms 1024 B apart.
+// Shared-memory matrix descriptor for a K-major operand without swizzle:
+// 8-row x 16-byte core matrices (rows 16 bytes apart), `lbo` bytes apart
+// along K and `sbo` bytes apart along M / N.
+__device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return uint64_t((addr & 0x3FFFF) >> 4) | (uint64_t(lbo >> 4) << 16)  // LBO: K direction
+           | (uint64_t(sbo >> 4) << 32)                                  // SBO: M direction
+           | (uint64_t(1) << 46);                                        // version; no swizzle
+}
+
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
     return uint64_t((addr & 0x3FFFF) >> 4) | (uint64_t(1) << 16)  // LBO (unused when swizzled)
            | (uint64_t(1024 >> 4) << 32)                            // SBO

@@ -1,5 +1,6 @@
 // TCA-TBE small-tile decoder of the fused GEMM: one thread rebuilds one 8x8
-// small tile (8 rows x 8 BF16) straight into a 128-byte-swizzled A tile.
+// small tile (8 rows x 8 BF16) straight into the A tile, where it is one
+// core matrix of the tensor cores' unswizzled K-major layout (zipgemm.cuh).
 //
 // Why a small tile per thread: inside a 64x64 tile the payload streams are
 // ordered band, column block j, row half, row, column (csrc/HostPacker.h:
@@ -11,9 +12,12 @@
 //
 // Lane mapping (warp q of a decoder group = 16-row band q of both tiles of
 // the row block): lane = tau*16 + rt*8 + j, i.e. tile tau, row half rt,
-// column block j. The thread writes chunk j of A rows 32q + 16tau + 8rt + r
-// (r = 0..7); the 8 lanes of one store phase write the 8 chunks of one row,
-// which the swizzle puts on distinct banks.
+// column block j. The thread writes the core matrix of A rows 32q + 16tau +
+// 8rt .. +7 and K chunk j: 128 contiguous bytes, row r at 16r and element
+// (r, c) at 2 * (8r + c), so its row stores take immediate offsets and a rare
+// element's address is its bit position times two. The 8 lanes of one store
+// phase write the 8 K chunks of one 8-row group, 2064 bytes apart: distinct
+// banks.
 //
 // Per row (8 elements): the three bitmap bytes (byte r of each plane word)
 // index a lookup table replicated per lane that spreads them to nibbles;
@@ -30,6 +34,7 @@
 
 #include "decode.cuh"
 #include "ptx.cuh"
+#include "zipgemm.cuh"
 
 namespace zs {
 
@@ -37,37 +42,20 @@ struct TileDecoder {
     uint32_t ct;        // shared address of the code table + (lane % kTableCopies) * 4
     uint32_t word;      // byte offset of this small tile's word in a tile's bitmap plane
     uint32_t band8;     // byte offset of band q's (common, rare) pair in a tile's band offsets
-    uint32_t jx;        // j << 4: this thread's 16-byte chunk before swizzling
-    uint32_t arow;      // offset of A row 32q + 16tau + 8rt in an A tile
+    uint32_t aoff;      // offset of this thread's core matrix in an A tile
     uint32_t ord64;     // 64 * (2j + rt): elements before this small tile in its band
     uint32_t j, rt;
-    uint32_t xp_lo, xp_hi;  // exponent palette (see RowDecoder)
-    uint32_t k2, k4, k8, kent, krank, khi;
 
-    __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int q,
-                                         uint32_t start_exp) {
+    __device__ __forceinline__ void init(uint32_t tables_smem, int lane, int q) {
         const uint32_t tau = uint32_t(lane) >> 4;
         rt = (uint32_t(lane) >> 3) & 1u;
         j = uint32_t(lane) & 7u;
         ct = tables_smem + uint32_t(lane % kTableCopies) * 4u;
         word = (uint32_t(q) * 16u + 2u * j + rt) * 8u;
         band8 = uint32_t(q) * 8u;
-        jx = j << 4;
-        const uint32_t row = uint32_t(32 * q) + 16u * tau + 8u * rt;  // multiple of 8
-        arow = (row >> 3) * 1024u;
+        // 8-row group (32q + 16tau + 8rt) / 8 along M, K chunk j.
+        aoff = (4u * uint32_t(q) + 2u * tau + rt) * kAGroup + j * kACoreK;
         ord64 = 64u * (2u * j + rt);
-        uint32_t xp[2] = {0, 0};
-        for (int c = 1; c < 8; ++c) {
-            const uint32_t e = (start_exp + uint32_t(c)) & 255u;
-            xp[c >> 2] |= (((e & 1u) << 7) | (e >> 1)) << (8 * (c & 3));
-        }
-        xp_lo = xp[0], xp_hi = xp[1];
-        k2 = ptx::launder(2u);
-        k4 = ptx::launder(4u);
-        k8 = ptx::launder(8u);
-        kent = ptx::launder(uint32_t(kTableCopies) * 4u);
-        krank = ptx::launder(0x11111110u);
-        khi = ptx::launder(0x10000u);
     }
 
     // Decode this thread's small tile of the tile whose slot data sits at
@@ -77,7 +65,11 @@ struct TileDecoder {
     // lanes call this together. cap_c / cap_r (bytes / words) bound the
     // offsets read from the packed data. A thread whose tile does not exist
     // (ragged last row block) passes valid = false and writes zeros.
-    __device__ __forceinline__ void decode_store(uint32_t plane, uint32_t plane_stride,
+    // `kc` holds the multipliers and the exponent palette (a DecodeConsts in
+    // the kernel's parameter bank).
+    template <class Consts>
+    __device__ __forceinline__ void decode_store(const Consts& kc, uint32_t plane,
+                                                 uint32_t plane_stride,
                                                  uint32_t medium, uint32_t common, uint32_t rare,
                                                  uint32_t cap_c, uint32_t cap_r, uint32_t atile,
                                                  bool valid) const {
@@ -97,16 +89,21 @@ struct TileDecoder {
             if (j >= d) incl += v;
         }
         const uint32_t before = incl - pair + (rt ? other : 0u);
+        // Trip counts of the rare patch loops below: the most rare elements
+        // any lane of the warp has in rows 0-3 and in rows 4-7 (a missing
+        // tile counts none). Every lane takes part, before the return below.
+        const uint32_t n_lo =
+            32u - uint32_t(__reduce_min_sync(kFullMask, valid ? uint32_t(__popc(ind_lo)) : 32u));
+        const uint32_t n_hi =
+            32u - uint32_t(__reduce_min_sync(kFullMask, valid ? uint32_t(__popc(ind_hi)) : 32u));
         const int2 med = ptx::lds_s64(medium + band8);
         const uint32_t cofs = min(uint32_t(max(med.x, 0)) + before, cap_c);
         const uint32_t rofs = min(uint32_t(max(med.y, 0)) + ord64 - before, cap_r);
         uint32_t co = common + cofs;
-        const uint32_t arow_s = atile + arow;
+        const uint32_t a_s = atile + aoff;
         if (!valid) {  // only in a ragged last row block: zero rows, no patches
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
-                ptx::sts128(arow_s + uint32_t(r) * 128u + (jx ^ (uint32_t(r) << 4)),
-                            make_uint4(0u, 0u, 0u, 0u));
+            for (int r = 0; r < 8; ++r) ptx::sts128(a_s + uint32_t(r) * 16u, make_uint4(0u, 0u, 0u, 0u));
             return;
         }
 #pragma unroll
@@ -115,23 +112,23 @@ struct TileDecoder {
             const uint32_t m1 = __byte_perm(r < 4 ? p1.x : p1.y, 0, sel);
             const uint32_t m2 = __byte_perm(r < 4 ? p2.x : p2.y, 0, sel);
             const uint32_t m3 = __byte_perm(r < 4 ? p3.x : p3.y, 0, sel);
-            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, kent, ct));
-            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, kent, ct));
-            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, kent, ct));
-            const uint32_t code = ptx::mad_lo(t3, k4, ptx::mad_lo(t2, k2, t1));
+            const uint32_t t1 = ptx::lds_s32(ptx::mad_lo(m1, kc.kent, ct));
+            const uint32_t t2 = ptx::lds_s32(ptx::mad_lo(m2, kc.kent, ct));
+            const uint32_t t3 = ptx::lds_s32(ptx::mad_lo(m3, kc.kent, ct));
+            const uint32_t code = ptx::mad_lo(t3, kc.k4, ptx::mad_lo(t2, kc.k2, t1));
             const uint32_t flag = t1 | t2 | t3;
             const uint32_t aw = co & ~3u;
             const uint32_t w0 = ptx::lds_s32(aw), w1 = ptx::lds_s32(aw + 4), w2 = ptx::lds_s32(aw + 8);
-            const uint32_t sh = ptx::mad_lo(co, k8, 0);
+            const uint32_t sh = ptx::mad_lo(co, kc.k8, 0);
             const uint32_t q0 = __funnelshift_r(w0, w1, sh);
             const uint32_t q1 = __funnelshift_r(w1, w2, sh);
             co += uint32_t(__popc(m1 | m2 | m3));
-            const uint32_t rank = ptx::mad_lo(flag, krank, 0);
-            const uint32_t rank_hi = ptx::mul_hi(rank, khi);
+            const uint32_t rank = ptx::mad_lo(flag, kc.krank, 0);
+            const uint32_t rank_hi = ptx::mul_hi(rank, kc.khi);
             uint32_t out[4];
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank);
-                const uint32_t xv = __byte_perm(xp_lo, xp_hi, code);
+                const uint32_t xv = __byte_perm(kc.xp_lo, kc.xp_hi, code);
                 const uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
                 const uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 out[0] = __byte_perm(a, b, 0x5140);
@@ -139,31 +136,42 @@ struct TileDecoder {
             }
             {
                 const uint32_t pe = __byte_perm(q0, q1, rank_hi);
-                const uint32_t xv = __byte_perm(xp_lo, xp_hi, ptx::mul_hi(code, khi));
+                const uint32_t xv = __byte_perm(kc.xp_lo, kc.xp_hi, ptx::mul_hi(code, kc.khi));
                 const uint32_t a = (pe & 0x7F7F7F7Fu) | (xv & 0x80808080u);
                 const uint32_t b = (pe & 0x80808080u) | (xv & 0x7F7F7F7Fu);
                 out[2] = __byte_perm(a, b, 0x5140);
                 out[3] = __byte_perm(a, b, 0x7362);
             }
-            ptx::sts128(arow_s + uint32_t(r) * 128u + (jx ^ (uint32_t(r) << 4)),
-                        make_uint4(out[0], out[1], out[2], out[3]));
+            ptx::sts128(a_s + uint32_t(r) * 16u, make_uint4(out[0], out[1], out[2], out[3]));
         }
         // Rare elements in row order: element p = 8r + c of the small tile is
-        // the next word of the tile's rare run.
-        uint32_t rlo = ~ind_lo, rhi = ~ind_hi;
-        uint32_t ri = rofs;
-        const uint32_t rcap = cap_r ? cap_r - 1 : 0;
-        while (rlo | rhi) {
-            const bool hi = rlo == 0u;
-            const uint32_t m = hi ? rhi : rlo;
-            const uint32_t p = uint32_t(__ffs(m) - 1) + (hi ? 32u : 0u);  // 0..63
-            const uint32_t m2 = m & (m - 1u);
-            rlo = hi ? rlo : m2;
-            rhi = hi ? m2 : rhi;
-            const uint32_t wv = ptx::lds_u16(ptx::mad_lo(min(ri, rcap), k2, rare));
-            ++ri;
-            const uint32_t r = p >> 3;
-            ptx::sts16(arow_s + r * 128u + ((jx ^ (r << 4)) | ((p & 7u) << 1)), wv);
+        // the next word of the tile's rare run, stored at 2p in the core
+        // matrix. Rows 0-3, then rows 4-7 (64 bytes further), each a loop of
+        // the warp's uniform trip count in which a lane patches its lowest
+        // remaining rare bit. The run is read from its clamped start without
+        // a per-word clamp: at most 64 words, which stay inside the slot ring
+        // and its pad.
+        uint32_t ra = rare + 2u * rofs;
+        uint32_t rm = ~ind_lo;
+        for (uint32_t i = 0; i < n_lo; ++i) {
+            if (rm) {
+                const uint32_t p = uint32_t(__ffs(rm) - 1);
+                rm &= rm - 1u;
+                const uint32_t wv = ptx::lds_u16(ra);
+                ra += 2u;
+                ptx::sts16(a_s + 2u * p, wv);
+            }
+        }
+        rm = ~ind_hi;
+        const uint32_t a_h = a_s + 64u;
+        for (uint32_t i = 0; i < n_hi; ++i) {
+            if (rm) {
+                const uint32_t p = uint32_t(__ffs(rm) - 1);
+                rm &= rm - 1u;
+                const uint32_t wv = ptx::lds_u16(ra);
+                ra += 2u;
+                ptx::sts16(a_h + 2u * p, wv);
+            }
         }
     }
 };

@@ -7,8 +7,9 @@
 // slices. Warp roles (1 CTA per SM):
 //   warp 0      allocates tensor memory and issues tcgen05.mma (one
 //               elected lane) with both operands in shared memory (A = a
-//               decoder group's tile of decoded W, B = an x tile, both
-//               128-byte swizzled) and two FP32 accumulators in TMEM;
+//               decoder group's tile of decoded W in the unswizzled
+//               core-matrix layout, B = an x tile, 128-byte swizzled as TMA
+//               writes it) and two FP32 accumulators in TMEM;
 //   warp 1      keeps a ring of x slices filled with 3-D TMA loads;
 //   warps 2-3   producers: fill the compressed ring's slots as soon as their
 //               previous K slice was decoded, with few, large copies (an
@@ -19,9 +20,9 @@
 //   warps 4..   NDG decoder groups of four warps. Group g decodes the CTA's
 //               K slices g, g+NDG, ... (slice t from ring entry t % nslots)
 //               into its A tile: warp q takes 16-row band q of both tiles,
-//               each thread rebuilds one 8x8 small tile (tile_decode.cuh)
-//               with 16-byte stores and patches its rare elements with
-//               16-bit stores;
+//               each thread rebuilds one 8x8 small tile (tile_decode.cuh),
+//               one core matrix of the A tile, with 16-byte stores and
+//               patches its rare elements with 16-bit stores;
 //   last 4      epilogue, one TMEM lane quarter each: TMEM -> BF16 -> y for
 //               whole units, TMEM -> FP32 pieces for split ones.
 // Split-K: the grid is persistent (one CTA per SM) and every CTA takes an
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         const int nx = p.nx, na = p.na;
         const bool xmerged = nx == na;
         const uint64_t xdesc0 = ptx::smem_desc_sw128(sbase + p.off_x);
-        const uint64_t adesc0 = ptx::smem_desc_sw128(sbase + p.off_a);
+        const uint64_t adesc0 = ptx::smem_desc_kmajor(sbase + p.off_a, kACoreK, kAGroup);
         const uint32_t x_lo0 = uint32_t(xdesc0), x_hi = uint32_t(xdesc0 >> 32);
         const uint32_t a_lo0 = uint32_t(adesc0), a_hi = uint32_t(adesc0 >> 32);
         const uint32_t xstep = p.x_bytes >> 4, astep = kATileBytes >> 4;
@@ -442,7 +443,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             ok = ptx::mbar_wait(bar_addr(bar_afull, a), aph) && ok;
             if (!__all_sync(kFullMask, ok)) break;
             ptx::tc_fence_after();
-            ptx::mma_bf16_slice_elect(tmem + uint32_t(s & 1) * tcols, a_lo, a_hi, x_lo, x_hi, idesc,
+            ptx::mma_bf16_slice_elect<2 * kACoreK / 16>(tmem + uint32_t(s & 1) * tcols, a_lo, a_hi, x_lo, x_hi, idesc,
                                       first ? 0u : 1u, bar_addr(bar_aempty, a));
             if (!xmerged) ptx::mma_commit_elect(bar_addr(bar_xempty, xs));
             if (last) ptx::mma_commit_elect(bar_addr(bar_d, s & 1));  // segment complete
@@ -613,7 +614,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         const int q = warp & 3;  // TMEM lane quarter of this warp = band it decodes
         const int tau = lane >> 4;
         TileDecoder dec;
-        dec.init(tables, lane, q, p.start_exp);
+        dec.init(tables, lane, q);
         const uint32_t abase = sbase + p.off_a;
         const int na = p.na;  // >= NDG
         bool ok = ptx::mbar_wait(bar_tab, 0);
@@ -638,7 +639,7 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
             if (!__all_sync(kFullMask, ok)) break;
             const uint32_t tile = uint32_t(tau * p.S + j);  // the tile's index in the slot
             const int2 h = ptx::lds_s64(slot + L.hdr + tile * 8u);
-            dec.decode_store(slot + tile * L.plane1, L.plane_stride, slot + L.med + tile * 32u,
+            dec.decode_store(p.dk, slot + tile * L.plane1, L.plane_stride, slot + L.med + tile * 32u,
                              slot + (tau ? L.common1 : L.common0) + uint32_t(h.x),
                              slot + (tau ? L.rare1 : L.rare0) + 2u * uint32_t(h.y), cap_c, cap_r,
                              abase + uint32_t(a) * kATileBytes, valid);
@@ -915,8 +916,8 @@ struct GemmLayout {
     int nx, nslots;
 };
 
-// Shared memory: barriers | lookup tables | A tiles (na 16 KB 128 x 64
-// BF16 tiles, 1024-aligned) | x ring (nx slots of bn*128
+// Shared memory: barriers | lookup tables | A tiles (na 16.1 KB 128 x 64
+// BF16 tiles) | x ring (1024-aligned, nx slots of bn*128
 // bytes) | compressed slots (2 * ndg / S, each S K slices: two K slices'
 // worth per decoder group) | pad. The x ring gets one slot per A tile when
 // they fit (then an x slot is freed by the same commit as its A tile), else
@@ -925,7 +926,7 @@ GemmLayout gemm_layout(int ndg, int na, int bn, uint32_t plane_pitch, uint32_t c
                        uint32_t cap_r, int smem_limit, int S) {
     GemmLayout l{};
     l.off_a = round_up(kBarrierBytes + kTableBytes, 1024);
-    l.off_x = l.off_a + uint32_t(na) * kATileBytes;
+    l.off_x = round_up(l.off_a + uint32_t(na) * kATileBytes, 1024);  // x tiles: 128-byte swizzle
     l.x_bytes = uint32_t(bn) * 128;
     l.slot = gemm_slot_layout(plane_pitch, cap_c, cap_r, S);
     // At least two K slices of compressed data per decoder group; the x ring
@@ -1286,6 +1287,17 @@ cudaError_t launch_zipgemm(cudaStream_t stream, const void* sm, const void* rare
     p.cap_c = common_capacity(max_common);
     p.cap_r = uint32_t(max_rare);
     p.start_exp = uint32_t(start_exp) & 255u;
+    {
+        // Exponent palette: byte c = exponent start_exp + c rotated right by
+        // one bit (bit 7 = its bit 0, bits 0-6 = its bits 1-7).
+        uint32_t xp[2] = {0, 0};
+        for (int c = 1; c < 8; ++c) {
+            const uint32_t e = (p.start_exp + uint32_t(c)) & 255u;
+            xp[c >> 2] |= (((e & 1u) << 7) | (e >> 1)) << (8 * (c & 3));
+        }
+        p.dk = DecodeConsts{2u, 4u, 8u, uint32_t(kTableCopies) * 4u, 0x11111110u, 0x10000u,
+                            xp[0], xp[1]};
+    }
     // Bitmap tensor maps. Equally spaced planes (one allocation, as the
     // runtime lays them out) load with one 4-D copy into a 528-byte pitch;
     // otherwise three copies need 128-byte aligned planes: pitch 576. 512

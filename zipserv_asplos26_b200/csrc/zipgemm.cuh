@@ -13,7 +13,16 @@ constexpr int kMaxATiles = 8;    // decoded A tiles (decoder groups x tiles per 
 constexpr int kBarrierBytes = 1024;
 constexpr int kChunk = 32;       // K slices per refill of the offset / band-offset caches
 constexpr int kMaxGroup = 8;     // tiles per half of a compressed ring slot
-constexpr uint32_t kATileBytes = 128 * 128;  // decoded A tile: 128 rows x 64 BF16
+// Decoded A tile: 128 rows x 64 BF16 in the tensor cores' K-major layout
+// without swizzle, built from "core matrices" of 8 rows x 8 BF16 (8 rows of
+// 16 bytes, 128 contiguous bytes, exactly one 8x8 small tile of the format).
+// The 16 core matrices of one K chunk (8 columns) are contiguous along M
+// (kAGroup = 128 bytes apart); the 8 K chunks are kACoreK = 2064 bytes
+// apart (2048 + 16), which puts the 8 core matrices of one 8-row group on
+// distinct banks.
+constexpr uint32_t kAGroup = 128;
+constexpr uint32_t kACoreK = 16 * kAGroup + 16;
+constexpr uint32_t kATileBytes = 7 * kACoreK + 16 * kAGroup + 16;  // 16512, a multiple of 128
 constexpr int kMaxTp = 8;        // ranks of a fused all-reduce
 
 // A compressed ring slot holds two runs ("halves") of up to kMaxGroup tiles
@@ -32,6 +41,16 @@ struct SlotLayout {
 };
 SlotLayout gemm_slot_layout(uint32_t plane_pitch, uint32_t cap_c, uint32_t cap_r, int S);
 SlotLayout decompress_slot_layout(int half, uint32_t cap_c, uint32_t cap_r);
+
+// Multipliers and the exponent palette of the small-tile decoder, kept in
+// the kernel's parameter (constant) bank: the decoder's multiply-adds take
+// them as constant-bank operands, so they run on the FMA pipe (a literal
+// would be strength-reduced to shifts on the integer ALU) without holding
+// registers.
+struct DecodeConsts {
+    uint32_t k2, k4, k8, kent, krank, khi;
+    uint32_t xp_lo, xp_hi;  // exponent palette (see RowDecoder)
+};
 
 struct GemmParams {
     const uint8_t* sm;
@@ -59,6 +78,7 @@ struct GemmParams {
                            // writes tile t % na
     uint32_t cap_c, cap_r;  // payload capacity per tile (bytes, words)
     uint32_t start_exp;
+    DecodeConsts dk;
     uint32_t plane_box_bytes;  // bytes one bitmap tensor load (or three) writes
     uint32_t off_a, off_x, off_slots;
     uint32_t x_bytes;      // one x slot: bn tokens x one K slice (bn * 128 bytes)
