@@ -5,7 +5,8 @@
 // Why a small tile per thread: inside a 64x64 tile the payload streams are
 // ordered band, column block j, row half, row, column (csrc/HostPacker.h:
 // 110-150), so a small tile's common bytes and rare words are each one
-// contiguous run. A thread walks its 8 rows with a running offset, needs one
+// contiguous run. A thread takes each row's offset in the run from a masked
+// population count of the small tile's bitmap OR, needs one
 // 16-lane scan per step (the small tiles of a band, in stream order) instead
 // of one per row, loads each bitmap plane as one 64-bit word, and patches its
 // rares from a plain running index.
@@ -99,7 +100,9 @@ struct TileDecoder {
         const int2 med = ptx::lds_s64(medium + band8);
         const uint32_t cofs = min(uint32_t(max(med.x, 0)) + before, cap_c);
         const uint32_t rofs = min(uint32_t(max(med.y, 0)) + ord64 - before, cap_r);
-        uint32_t co = common + cofs;
+        // Row r's payload starts after the commons of rows 0 .. r-1: one
+        // masked population count per row, so no row waits for the previous.
+        const uint32_t co0 = common + cofs, co4 = co0 + uint32_t(__popc(ind_lo));
         const uint32_t a_s = atile + aoff;
         if (!valid) {  // only in a ragged last row block: zero rows, no patches
 #pragma unroll
@@ -108,6 +111,11 @@ struct TileDecoder {
         }
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
+            const uint32_t co =
+                (r & 3) == 0 ? (r ? co4 : co0)
+                             : (r < 4 ? co0 : co4) +
+                                   uint32_t(__popc((r < 4 ? ind_lo : ind_hi) &
+                                                   ((1u << (8 * (r & 3))) - 1u)));
             const uint32_t sel = 0x4440u | uint32_t(r & 3);
             const uint32_t m1 = __byte_perm(r < 4 ? p1.x : p1.y, 0, sel);
             const uint32_t m2 = __byte_perm(r < 4 ? p2.x : p2.y, 0, sel);
@@ -122,7 +130,6 @@ struct TileDecoder {
             const uint32_t sh = ptx::mad_lo(co, kc.k8, 0);
             const uint32_t q0 = __funnelshift_r(w0, w1, sh);
             const uint32_t q1 = __funnelshift_r(w1, w2, sh);
-            co += uint32_t(__popc(m1 | m2 | m3));
             const uint32_t rank = ptx::mad_lo(flag, kc.krank, 0);
             const uint32_t rank_hi = ptx::mul_hi(rank, kc.khi);
             uint32_t out[4];
@@ -148,30 +155,29 @@ struct TileDecoder {
         // the next word of the tile's rare run, stored at 2p in the core
         // matrix. Rows 0-3, then rows 4-7 (64 bytes further), each a loop of
         // the warp's uniform trip count in which a lane patches its lowest
-        // remaining rare bit. The run is read from its clamped start without
-        // a per-word clamp: at most 64 words, which stay inside the slot ring
-        // and its pad.
+        // remaining rare bit (a lane with none left reads a word it does not
+        // store). The run is read from its clamped start without a per-word
+        // clamp: at most 65 words, which stay inside the slot ring and its
+        // pad.
         uint32_t ra = rare + 2u * rofs;
         uint32_t rm = ~ind_lo;
         for (uint32_t i = 0; i < n_lo; ++i) {
-            if (rm) {
-                const uint32_t p = uint32_t(__ffs(rm) - 1);
-                rm &= rm - 1u;
-                const uint32_t wv = ptx::lds_u16(ra);
-                ra += 2u;
-                ptx::sts16(a_s + 2u * p, wv);
-            }
+            const bool has = rm != 0u;
+            const uint32_t p = uint32_t(__ffs(rm) - 1);
+            rm &= rm - 1u;
+            const uint32_t wv = ptx::lds_u16(ra);
+            if (has) ptx::sts16(a_s + 2u * p, wv);
+            ra += has ? 2u : 0u;
         }
         rm = ~ind_hi;
         const uint32_t a_h = a_s + 64u;
         for (uint32_t i = 0; i < n_hi; ++i) {
-            if (rm) {
-                const uint32_t p = uint32_t(__ffs(rm) - 1);
-                rm &= rm - 1u;
-                const uint32_t wv = ptx::lds_u16(ra);
-                ra += 2u;
-                ptx::sts16(a_h + 2u * p, wv);
-            }
+            const bool has = rm != 0u;
+            const uint32_t p = uint32_t(__ffs(rm) - 1);
+            rm &= rm - 1u;
+            const uint32_t wv = ptx::lds_u16(ra);
+            if (has) ptx::sts16(a_h + 2u * p, wv);
+            ra += has ? 2u : 0u;
         }
     }
 };

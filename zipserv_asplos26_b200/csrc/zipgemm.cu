@@ -630,6 +630,10 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
         // v / nslots, all advanced without divisions.
         const int S = p.S, nslots = p.nslots;
         int j = g % S, sidx = (g / S) % nslots, use = (g / S) / nslots;
+        // Per step the group moves NDG slices on: NDG / S slots plus NDG % S
+        // slices (one more slot when the slice index wraps); NDG <= nslots,
+        // so the ring index wraps at most once.
+        const int dslot = NDG / S, dj = NDG % S;
         for (int t = g; t < nsteps; t += NDG) {
             const bool valid = tau == 0 || 2 * rb + 1 < p.row_tiles;
             const uint32_t slot = ptx::launder(sbase + p.off_slots + uint32_t(sidx) * L.bytes);
@@ -651,10 +655,9 @@ __global__ void __launch_bounds__(256 + 128 * NDG, 1)
                 ptx::mbar_arrive(bar_addr(bar_afull, a));
             }
             if ((a += NDG) >= na) a -= na, ++ause;
-            for (j += NDG; j >= S;) {
-                j -= S;
-                if (++sidx == nslots) sidx = 0, ++use;
-            }
+            int adv = dslot;
+            if ((j += dj) >= S) j -= S, ++adv;
+            if ((sidx += adv) >= nslots) sidx -= nslots, ++use;
             for (k += NDG; k >= kt;) {
                 k -= kt;
                 if (++rb == rbs) rb = 0;
