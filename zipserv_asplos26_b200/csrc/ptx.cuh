@@ -386,9 +386,6 @@ __host__ __device__ constexpr uint32_t idesc_bf16_m128(uint32_t n) {
            | ((128u >> 4) << 24);  // M / 16
 }
 
-// Shared-memory matrix descriptor for a K-major operand stored in the
-// 128-byte-swizzled layout TMA writes for a 64-element (128 B) BF16 box
-// width: 8-row x 128 B atoms, atoms 1024 B apart.
 // Shared-memory matrix descriptor for a K-major operand without swizzle:
 // 8-row x 16-byte core matrices (rows 16 bytes apart), `lbo` bytes apart
 // along K and `sbo` bytes apart along M / N.
@@ -398,6 +395,9 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t addr, uint32_t lbo
            | (uint64_t(1) << 46);                                        // version; no swizzle
 }
 
+// Shared-memory matrix descriptor for a K-major operand stored in the
+// 128-byte-swizzled layout TMA writes for a 64-element (128 B) BF16 box
+// width: 8-row x 128 B atoms, atoms 1024 B apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
     return uint64_t((addr & 0x3FFFF) >> 4) | (uint64_t(1) << 16)  // LBO (unused when swizzled)
            | (uint64_t(1024 >> 4) << 32)                            // SBO
