@@ -1,7 +1,7 @@
 """The Llama-3 decode-step workload (zipserv_asplos26_b200.llama_decode, the
 benchmarked decode-step model) at a reduced shape.
 
-CPU (gloo, two ranks): the Megatron split of the step — qkv by heads,
+CPU (gloo, two and four ranks): the Megatron split of the step — qkv by heads,
 gate_up by intermediate rows, o and down on K with an all-reduce, the
 lm_head by vocabulary rows with a padded last shard — reproduces the
 single-rank logits and greedy tokens of the same seeded model (dense
@@ -25,6 +25,10 @@ from zipserv_asplos26_b200.llama_decode import DecodeStep, LlamaShape
 
 SMALL = LlamaShape(layers=2, hidden=256, heads=8, kv_heads=2, head_dim=32, ffn=512,
                    vocab=1000, context=64)
+# Four KV heads so the heads split four ways (the benchmarked model has 8 KV
+# heads, which split up to TP 8).
+SMALL4 = LlamaShape(layers=2, hidden=256, heads=8, kv_heads=4, head_dim=32, ffn=512,
+                    vocab=1000, context=64)
 TOKENS = [3, 141, 592, 653, 589, 793]
 
 
@@ -34,12 +38,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, results):
+def _rank_main(rank, world, port, results, shape=SMALL):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        model = DecodeStep(SMALL, len(TOKENS), "cpu", mode="dense", world=world, rank=rank)
+        model = DecodeStep(shape, len(TOKENS), "cpu", mode="dense", world=world, rank=rank)
         tokens = torch.tensor(TOKENS)
         logits = model.logits(tokens)
         parts = [torch.empty_like(logits) for _ in range(world)]
@@ -47,29 +51,30 @@ def _rank_main(rank, world, port, results):
         # the step issues its own collectives; every rank takes part
         nxt = model.step(tokens)
         if rank == 0:
-            results[world] = (torch.cat(parts, dim=1)[:, :SMALL.vocab], nxt)
+            results[world] = (torch.cat(parts, dim=1)[:, :shape.vocab], nxt)
     finally:
         dist.destroy_process_group()
 
 
-def _run(world):
+def _run(world, shape=SMALL):
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
-    mp.start_processes(_rank_main, args=(world, _free_port(), results), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), results, shape), nprocs=world,
                        start_method="spawn", join=True)
     return results[world]
 
 
-def test_tensor_parallel_step_matches_one_rank():
-    one_logits, one_next = _run(1)
-    two_logits, two_next = _run(2)
+@pytest.mark.parametrize("world,shape", [(2, SMALL), (4, SMALL4)])
+def test_tensor_parallel_step_matches_one_rank(world, shape):
+    one_logits, one_next = _run(1, shape)
+    tp_logits, tp_next = _run(world, shape)
     scale = one_logits.abs().max()
-    assert (two_logits - one_logits).abs().max() / scale < 2e-2
+    assert (tp_logits - one_logits).abs().max() / scale < 2e-2
     # Greedy tokens agree wherever the top-2 margin exceeds the rounding noise.
     top2 = one_logits.topk(2, dim=-1).values
     clear = (top2[:, 0] - top2[:, 1]) > 5e-2 * scale
     assert clear.any()
-    assert torch.equal(one_next[clear], two_next[clear])
+    assert torch.equal(one_next[clear], tp_next[clear])
 
 
 @pytest.mark.gpu

@@ -1,4 +1,4 @@
-"""Tensor-parallel host logic on two CPU ranks (gloo): shard boundaries,
+"""Tensor-parallel host logic on two and four CPU ranks (gloo): shard boundaries,
 per-rank packing of its own shard, column outputs concatenating to the full
 product and row partials all-reduced to it. The per-rank multiply is the
 CPU oracle (decode + FP32 GEMM) standing in for the CUDA kernel, so the test
@@ -17,9 +17,6 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from zipserv_asplos26_b200 import runtime, tp
-
-WORLD = 2
-
 
 def _free_port() -> int:
     with socket.socket() as s:
@@ -45,9 +42,9 @@ def _weights(m, k, n):
     return w, x
 
 
-def _rank_main(rank, port, results):
+def _rank_main(rank, world, port, results):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD,
+    dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     try:
         from oracle import oracle
@@ -56,10 +53,10 @@ def _rank_main(rank, port, results):
         out = {}
         for kind, (m, k) in (("column", (256, 384)), ("row", (192, 512))):
             w, x = _weights(m, k, 5)
-            layer = tp.ParallelLinear.from_weight(w, kind, WORLD, rank, "cpu")
+            layer = tp.ParallelLinear.from_weight(w, kind, world, rank, "cpu")
             y = layer.forward(x, linear=_oracle_linear)
             if kind == "column":
-                parts = [torch.empty_like(y) for _ in range(WORLD)]
+                parts = [torch.empty_like(y) for _ in range(world)]
                 dist.all_gather(parts, y)
                 y = torch.cat(parts, dim=-1)
             full = _oracle_linear(x, runtime.compress(w))
@@ -71,12 +68,14 @@ def _rank_main(rank, port, results):
         dist.destroy_process_group()
 
 
-def test_two_rank_column_and_row_parallel(native_lib, oracle_mod):
+@pytest.mark.parametrize("world", [2, 4])
+def test_column_and_row_parallel(native_lib, oracle_mod, world):
     ctx = mp.get_context("spawn")
     manager = ctx.Manager()
     results = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, port, results)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, results))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -84,12 +83,13 @@ def test_two_rank_column_and_row_parallel(native_lib, oracle_mod):
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    for r in range(WORLD):
+    for r in range(world):
         res = results[r]
-        # Column: every rank's M/2 rows concatenate to the full product exactly.
-        assert res["column"] == 0.0 and res["column_local_m"] == 128
+        # Column: every rank's M/world rows concatenate to the full product exactly.
+        assert res["column"] == 0.0 and res["column_local_m"] == 256 // world
         # Row: FP32 partial sums reordered by the K split only.
-        assert res["row"] < 1e-5 and res["row_local_k"] == 256 and res["row_local_m"] == 192
+        assert res["row"] < 1e-5 and res["row_local_k"] == 512 // world
+        assert res["row_local_m"] == 192
 
 
 def test_shard_bounds_reject_unaligned_splits():
